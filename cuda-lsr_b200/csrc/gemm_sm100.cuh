@@ -1,0 +1,444 @@
+// Persistent, warp-specialised tcgen05 GEMM engine for sm_100a.
+//
+//   D[g][b] (tile of BM x BN) = sum over segments s of  opA_s[b] * opB_s[b]^T
+//
+// * one CTA per SM (persistent), tiles handed out round-robin over a flat list
+//   that spans up to kMaxGroups independent problem groups (e.g. the four
+//   parameter shapes of a model), each a batch of equally shaped matrices;
+// * warp 0   : TMA producer (one elected thread), STAGES-deep smem ring;
+// * warp 1   : owns TMEM (512 columns = two BN-wide fp32 accumulators) and one
+//              thread issues tcgen05.mma (M=128, N=BN, K=16) per 16-wide K step;
+// * warps 2-5: epilogue; each warp drains its 32 TMEM lanes with tcgen05.ld
+//              while the MMA warp already accumulates the next tile into the
+//              other accumulator.
+// * operands are bf16 (or tf32) in 128-byte-swizzled smem tiles, either K-major
+//   (TMA box 64 x rows) or MN-major (TMA boxes 64 x 64); a segment list lets one
+//   accumulator sum two products (A*X + X*B^T for the Kronecker sum).
+// * triangle mode computes only tiles touching the upper triangle of a
+//   symmetric square output and mirrors each element into the lower triangle.
+//
+// No cluster multicast is used anywhere: every CTA loads its own tiles.
+#pragma once
+
+#include "lsr_common.cuh"
+
+namespace lsr {
+
+constexpr int kMaxGroups = 4;
+constexpr int kMaxSeg = 2;
+constexpr int BM = 128;
+constexpr int BK = 64;  // bf16 elements in one 128-byte swizzle row
+constexpr int kGemmThreads = 192;
+constexpr int kEpiThreads = 128;
+
+// Epilogue modes.
+enum : int {
+  EPI_STORE_BF16 = 0,  // out = bf16(alpha * acc)
+  EPI_STORE_F32 = 1,   // out = alpha * acc
+  EPI_NS_GRAM = 2,     // out = bf16(acc)                                  (symmetric)
+  EPI_NS_POLY = 3,     // out = bf16(bf16(alpha*aux) + bf16(beta*bf16(acc))) (symmetric)
+  EPI_NS_UPDATE = 4,   // out = bf16(bf16(alpha*aux) + bf16(acc))
+  EPI_F32_EMA = 5,     // out = beta * out + alpha * acc                     (fp32)
+};
+
+struct SegDesc {
+  int kblocks;   // number of BK-wide K blocks
+  int a_mn;      // operand A stored MN-major (rows of A are columns in memory)
+  int b_mn;      // operand B stored MN-major
+  int a_bcast;   // operand A is shared by the whole batch (TMA z = 0)
+  int b_bcast;
+};
+
+struct GroupDesc {
+  int batch, M, N;
+  int tiles_m, tiles_n, tiles_per_mat, tile_begin;
+  int tri;  // symmetric output: upper-triangle tiles only, mirrored stores
+  int nseg;
+  SegDesc seg[kMaxSeg];
+  void* out;
+  long long out_bs;  // batch stride in elements
+  int ldo;
+  int out_trans;  // store element (r, c) at out[c * ldo + r]
+  const void* aux;
+  long long aux_bs;
+  int ld_aux;
+  float alpha, beta;
+};
+
+struct GemmParams {
+  CUtensorMap mapA[kMaxGroups][kMaxSeg];
+  CUtensorMap mapB[kMaxGroups][kMaxSeg];
+  GroupDesc g[kMaxGroups];
+  int ngroups;
+  int total_tiles;
+  int* status;
+};
+
+template <int BN>
+__host__ __device__ constexpr int tri_first_col_tile(int ti) {
+  return (ti * BM) / BN;
+}
+
+// Map a flat tile index to (group, batch entry, tile row, tile column).
+template <int BN>
+__device__ __forceinline__ void decode_tile(const GemmParams& p, int t, int& g, int& b, int& ti, int& tj) {
+  g = 0;
+#pragma unroll 1
+  while (g + 1 < p.ngroups && t >= p.g[g + 1].tile_begin) ++g;
+  const GroupDesc& G = p.g[g];
+  int local = t - G.tile_begin;
+  b = local / G.tiles_per_mat;
+  int r = local - b * G.tiles_per_mat;
+  if (!G.tri) {
+    ti = r / G.tiles_n;
+    tj = r - ti * G.tiles_n;
+  } else {
+    ti = 0;
+    tj = 0;
+#pragma unroll 1
+    for (; ti < G.tiles_m; ++ti) {
+      const int cnt = max(0, G.tiles_n - tri_first_col_tile<BN>(ti));
+      if (r < cnt) {
+        tj = tri_first_col_tile<BN>(ti) + r;
+        break;
+      }
+      r -= cnt;
+    }
+  }
+}
+
+// Status codes written when a bounded wait gives up.
+enum : int {
+  ST_TIMEOUT_PRODUCER = 101,
+  ST_TIMEOUT_MMA_FULL = 102,
+  ST_TIMEOUT_MMA_TMEM = 103,
+  ST_TIMEOUT_EPILOGUE = 104,
+  ST_TIMEOUT_TEARDOWN = 105,
+};
+
+// ---------------------------------------------------------------------------
+// Epilogue: one thread owns one output row and 32 consecutive columns.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, bool vec, int ncols, float (&v)[32]) {
+  if (vec && ncols >= 32) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 u = __ldg(s4 + q);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __bfloat1622float2(h[e]);
+        v[q * 8 + 2 * e] = f.x;
+        v[q * 8 + 2 * e + 1] = f.y;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (j < ncols) ? __bfloat162float(src[j]) : 0.f;
+  }
+}
+
+// Store 32 bf16 values of one row; only columns j with lo <= j < ncols are written.
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, bool vec, int lo, int ncols,
+                                              const float (&v)[32]) {
+  if (vec && lo <= 0 && ncols >= 32) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 u;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
+      d4[q] = u;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j >= lo && j < ncols) dst[j] = __float2bfloat16_rn(v[j]);
+  }
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const GroupDesc& G, int b, int row, int col0,
+                                               const uint32_t (&r)[32]) {
+  if (row >= G.M) return;
+  const int ncols = min(32, G.N - col0);
+  if (ncols <= 0) return;
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+
+  // Triangle mode: the thread writes columns c >= row directly and mirrors c > row.
+  const int lo = G.tri ? max(0, row - col0) : 0;
+  if (lo >= ncols) return;
+
+  if constexpr (EPI == EPI_STORE_F32 || EPI == EPI_F32_EMA) {
+    float* out = reinterpret_cast<float*>(G.out) + (long long)b * G.out_bs;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < lo || j >= ncols) continue;
+      const int c = col0 + j;
+      float val = G.alpha * v[j];
+      long long idx = G.out_trans ? (long long)c * G.ldo + row : (long long)row * G.ldo + c;
+      if constexpr (EPI == EPI_F32_EMA) {
+        if (G.beta != 0.f) val = fmaf(G.beta, out[idx], val);
+      }
+      out[idx] = val;
+      if (G.tri && c > row) out[(long long)c * G.ldo + row] = val;
+    }
+    return;
+  } else {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(G.out) + (long long)b * G.out_bs;
+    if constexpr (EPI == EPI_STORE_BF16) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = G.alpha * v[j];
+    } else if constexpr (EPI == EPI_NS_GRAM) {
+      // value = bf16(acc): rounding happens in the store
+    } else if constexpr (EPI == EPI_NS_POLY || EPI == EPI_NS_UPDATE) {
+      const __nv_bfloat16* aux =
+          reinterpret_cast<const __nv_bfloat16*>(G.aux) + (long long)b * G.aux_bs + (long long)row * G.ld_aux + col0;
+      const bool avec = ((G.ld_aux & 7) == 0) && ((reinterpret_cast<uintptr_t>(aux) & 15) == 0);
+      float x[32];
+      load_bf16x32(aux, avec, ncols, x);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if constexpr (EPI == EPI_NS_POLY)
+          v[j] = bf16r(G.alpha * x[j]) + bf16r(G.beta * bf16r(v[j]));
+        else
+          v[j] = bf16r(G.alpha * x[j]) + bf16r(v[j]);
+      }
+    }
+    if (!G.out_trans) {
+      __nv_bfloat16* dst = out + (long long)row * G.ldo + col0;
+      const bool vec = ((G.ldo & 7) == 0) && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
+      store_bf16x32(dst, vec, lo, ncols, v);
+    } else {
+      // transposed store: lanes of a warp hold consecutive rows, so each
+      // column j is one coalesced 64-byte segment.
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j >= lo && j < ncols) out[(long long)(col0 + j) * G.ldo + row] = __float2bfloat16_rn(v[j]);
+    }
+    if (G.tri) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int c = col0 + j;
+        if (j < ncols && c > row) out[(long long)c * G.ldo + row] = __float2bfloat16_rn(v[j]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The kernel
+// ---------------------------------------------------------------------------
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 5) + 16;
+  static constexpr int TOTAL = BAR_OFFSET + BAR_BYTES + 1024;  // + alignment slack
+};
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __grid_constant__ GemmParams p) {
+  static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 64 in [64, 256]");
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFFSET);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done_bar = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull + a, 1);
+      mbar_init(tempty + a, kEpiThreads);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    for (int g = 0; g < p.ngroups; ++g)
+      for (int s = 0; s < p.g[g].nseg; ++s) {
+        tma_prefetch_desc(&p.mapA[g][s]);
+        tma_prefetch_desc(&p.mapB[g][s]);
+      }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+        int g, b, ti, tj;
+        decode_tile<BN>(p, t, g, b, ti, tj);
+        const GroupDesc& G = p.g[g];
+        const int m0 = ti * BM, n0 = tj * BN;
+        for (int sg = 0; ok && sg < G.nseg; ++sg) {
+          const SegDesc S = G.seg[sg];
+          const CUtensorMap* ma = &p.mapA[g][sg];
+          const CUtensorMap* mb = &p.mapB[g][sg];
+          const int za = S.a_bcast ? 0 : b;
+          const int zb = S.b_bcast ? 0 : b;
+          for (int kb = 0; kb < S.kblocks; ++kb) {
+            if (!mbar_wait(empty + s, ph ^ 1, abort_flag, p.status, ST_TIMEOUT_PRODUCER)) {
+              ok = false;
+              break;
+            }
+            uint8_t* sa = smem + s * L::STAGE_BYTES;
+            uint8_t* sb = sa + L::A_BYTES;
+            mbar_arrive_expect_tx(full + s, L::STAGE_BYTES);
+            const int k0 = kb * BK;
+            if (!S.a_mn) {
+              tma_load_3d(sa, ma, full + s, k0, m0, za);
+            } else {
+#pragma unroll
+              for (int c = 0; c < BM / 64; ++c) tma_load_3d(sa + c * 8192, ma, full + s, m0 + 64 * c, k0, za);
+            }
+            if (!S.b_mn) {
+              tma_load_3d(sb, mb, full + s, k0, n0, zb);
+            } else {
+#pragma unroll
+              for (int c = 0; c < BN / 64; ++c) tma_load_3d(sb + c * 8192, mb, full + s, n0 + 64 * c, k0, zb);
+            }
+            if (++s == STAGES) {
+              s = 0;
+              ph ^= 1;
+            }
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t aph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+        int g, b, ti, tj;
+        decode_tile<BN>(p, t, g, b, ti, tj);
+        const GroupDesc& G = p.g[g];
+        if (!mbar_wait(tempty + acc, aph ^ 1, abort_flag, p.status, ST_TIMEOUT_MMA_TMEM)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        uint32_t accumulate = 0;
+        for (int sg = 0; ok && sg < G.nseg; ++sg) {
+          const SegDesc S = G.seg[sg];
+          const uint32_t idesc = make_idesc(BM, BN, 1u, (uint32_t)S.a_mn, (uint32_t)S.b_mn);
+          // per-UMMA_K (16 elements) descriptor advance, in 16-byte units
+          const uint32_t a_step = S.a_mn ? (2048u >> 4) : (32u >> 4);
+          const uint32_t b_step = S.b_mn ? (2048u >> 4) : (32u >> 4);
+          for (int kb = 0; kb < S.kblocks; ++kb) {
+            if (!mbar_wait(full + s, ph, abort_flag, p.status, ST_TIMEOUT_MMA_FULL)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(smem + s * L::STAGE_BYTES);
+            const uint32_t sb = sa + L::A_BYTES;
+            const uint64_t adesc = S.a_mn ? smem_desc_sw128(sa, 8192, 1024) : smem_desc_sw128(sa, 16, 1024);
+            const uint64_t bdesc = S.b_mn ? smem_desc_sw128(sb, 8192, 1024) : smem_desc_sw128(sb, 16, 1024);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              umma_bf16(d_tmem, adesc + (uint64_t)(k * a_step), bdesc + (uint64_t)(k * b_step), idesc, accumulate);
+              accumulate = 1;
+            }
+            umma_commit(empty + s);  // frees this smem stage once the MMAs have read it
+            if (++s == STAGES) {
+              s = 0;
+              ph ^= 1;
+            }
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull + acc);  // accumulator ready for the epilogue
+        acc ^= 1;
+        if (acc == 0) aph ^= 1;
+      }
+      // Drain: make sure no MMA is still writing TMEM before it is released.
+      umma_commit(done_bar);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(done_bar, 0)) {
+        if (globaltimer_ns() - t0 > LSR_WAIT_TIMEOUT_NS) {
+          set_status(p.status, ST_TIMEOUT_TEARDOWN);
+          break;
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t aph = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+      int g, b, ti, tj;
+      decode_tile<BN>(p, t, g, b, ti, tj);
+      const GroupDesc& G = p.g[g];
+      if (!mbar_wait(tfull + acc, aph, abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      const int row0 = ti * BM + q * 32;  // first row of this warp
+      const int row = row0 + lane;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const bool warp_rows_live = row0 < G.M;
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        const int col0 = tj * BN + cc * 32;
+        // warp-uniform skips: columns past N, or (triangle) chunk fully below the diagonal
+        if (!warp_rows_live || col0 >= G.N) continue;
+        if (G.tri && col0 + 31 < row0) continue;
+        uint32_t r[32];
+        tmem_ld32(tbase + static_cast<uint32_t>(cc * 32), r);
+        tmem_ld_wait();
+        epilogue_chunk<EPI>(G, b, row, col0, r);
+      }
+      tc_fence_before();
+      mbar_arrive(tempty + acc);
+      acc ^= 1;
+      if (acc == 0) aph ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace lsr

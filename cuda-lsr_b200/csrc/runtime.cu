@@ -1,0 +1,200 @@
+// Library runtime: version, error strings, device status word, TMA tensor-map
+// encoding through the driver entry point (no link-time libcuda dependency).
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "runtime.cuh"
+
+namespace lsr {
+
+// Device status word: 0 = no failure; otherwise the first failure code a
+// kernel recorded (e.g. a bounded wait that timed out).
+__device__ int g_status_word;
+
+namespace {
+constexpr int kMaxDevices = 64;
+int* g_status_cache[kMaxDevices] = {nullptr};
+int g_sm_cache[kMaxDevices] = {0};
+int g_cc_cache[kMaxDevices] = {0};
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+
+int current_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kMaxDevices) return -1;
+  return d;
+}
+std::atomic<long long> g_launches{0};
+
+struct ProfRec {
+  int kind;
+  cudaEvent_t a, b;
+};
+std::atomic<bool> g_prof_on{false};
+std::mutex g_prof_mu;
+std::vector<ProfRec> g_prof_open;   // begun, waiting for end (per kind, last one)
+std::vector<ProfRec> g_prof_done;
+std::vector<cudaEvent_t> g_prof_pool;
+
+cudaEvent_t take_event() {
+  if (!g_prof_pool.empty()) {
+    cudaEvent_t e = g_prof_pool.back();
+    g_prof_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+}  // namespace
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+void prof_begin(int kind, cudaStream_t st) {
+  if (!g_prof_on.load(std::memory_order_relaxed)) return;
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  ProfRec r{kind, take_event(), nullptr};
+  if (r.a) cudaEventRecord(r.a, st);
+  g_prof_open.push_back(r);
+}
+
+void prof_end(int kind, cudaStream_t st) {
+  if (!g_prof_on.load(std::memory_order_relaxed)) return;
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  for (size_t i = g_prof_open.size(); i-- > 0;) {
+    if (g_prof_open[i].kind != kind) continue;
+    ProfRec r = g_prof_open[i];
+    g_prof_open.erase(g_prof_open.begin() + (long)i);
+    r.b = take_event();
+    if (r.b) cudaEventRecord(r.b, st);
+    g_prof_done.push_back(r);
+    return;
+  }
+}
+
+int* status_ptr() {
+  const int d = current_device();
+  if (d < 0) return nullptr;
+  if (!g_status_cache[d]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
+    g_status_cache[d] = static_cast<int*>(p);
+  }
+  return g_status_cache[d];
+}
+
+int device_sm_count() {
+  const int d = current_device();
+  if (d < 0) return 1;
+  if (!g_sm_cache[d]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
+    g_sm_cache[d] = n > 0 ? n : 1;
+  }
+  return g_sm_cache[d];
+}
+
+int check_device() {
+  const int d = current_device();
+  if (d < 0) return LSR_ERR_DEVICE;
+  if (!g_cc_cache[d]) {
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, d) != cudaSuccess) return LSR_ERR_DEVICE;
+    g_cc_cache[d] = major;
+  }
+  return g_cc_cache[d] == 10 ? LSR_OK : LSR_ERR_DEVICE;
+}
+
+int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t inner,
+                   uint64_t outer, uint64_t batch, uint64_t ld, uint64_t bstride, uint32_t box_inner,
+                   uint32_t box_outer) {
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return LSR_ERR_DRIVER;
+    g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  // TMA requirements: 16-byte aligned base and strides.
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * elem_bytes) & 15) || ((bstride * elem_bytes) & 15))
+    return LSR_ERR_SHAPE;
+  cuuint64_t dims[3] = {inner, outer, batch};
+  cuuint64_t strides[2] = {ld * elem_bytes, bstride * elem_bytes};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, dtype, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LSR_OK : LSR_ERR_DRIVER;
+}
+
+}  // namespace lsr
+
+extern "C" {
+
+const char* lsr_version(void) { return "lsr-b200 0.1.0 (sm_100a)"; }
+
+const char* lsr_strerror(int code) {
+  switch (code) {
+    case LSR_OK: return "ok";
+    case LSR_ERR_ARG: return "invalid argument";
+    case LSR_ERR_SHAPE: return "unsupported shape, stride or alignment";
+    case LSR_ERR_WORKSPACE: return "workspace missing or too small";
+    case LSR_ERR_LAUNCH: return "kernel launch failed";
+    case LSR_ERR_DRIVER: return "TMA tensor map encoding failed";
+    case LSR_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
+    default: return "unknown liblsr error";
+  }
+}
+
+long long lsr_launch_count(void) { return lsr::g_launches.load(); }
+
+int lsr_profile_enable(int on) {
+  lsr::g_prof_on.store(on != 0);
+  return LSR_OK;
+}
+
+int lsr_profile_read(double* ms, long long* launches, int nkinds, int reset) {
+  if (nkinds < 0 || (nkinds > 0 && (!ms || !launches))) return LSR_ERR_ARG;
+  for (int k = 0; k < nkinds; ++k) {
+    ms[k] = 0.0;
+    launches[k] = 0;
+  }
+  std::lock_guard<std::mutex> lk(lsr::g_prof_mu);
+  for (const auto& r : lsr::g_prof_done) {
+    float t = 0.f;
+    if (r.a && r.b && cudaEventSynchronize(r.b) == cudaSuccess && cudaEventElapsedTime(&t, r.a, r.b) == cudaSuccess &&
+        r.kind < nkinds) {
+      ms[r.kind] += t;
+      launches[r.kind] += 1;
+    }
+  }
+  if (reset) {
+    for (auto& r : lsr::g_prof_done) {
+      if (r.a) lsr::g_prof_pool.push_back(r.a);
+      if (r.b) lsr::g_prof_pool.push_back(r.b);
+    }
+    lsr::g_prof_done.clear();
+  }
+  return LSR_OK;
+}
+
+int lsr_device_status(int* code, int clear) {
+  if (!code) return LSR_ERR_ARG;
+  int* p = lsr::status_ptr();
+  if (!p) return LSR_ERR_DEVICE;
+  if (cudaDeviceSynchronize() != cudaSuccess) return LSR_ERR_LAUNCH;
+  if (cudaMemcpy(code, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return LSR_ERR_LAUNCH;
+  if (clear && cudaMemset(p, 0, sizeof(int)) != cudaSuccess) return LSR_ERR_LAUNCH;
+  return LSR_OK;
+}
+
+}  // extern "C"

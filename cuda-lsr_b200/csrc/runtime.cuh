@@ -1,0 +1,115 @@
+// Host-side runtime helpers shared by the liblsr translation units.
+#pragma once
+
+#include <algorithm>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "gemm_sm100.cuh"
+
+namespace lsr {
+
+// Status word of the current device (device pointer), or nullptr on failure.
+int* status_ptr();
+// Number of SMs of the current device.
+int device_sm_count();
+// LSR_OK if the current device is sm_100 (B200 class).
+int check_device();
+
+// Encode a 3-D bf16 tensor map over [batch][outer][inner] with row stride
+// `ld` and batch stride `bstride` (elements), 128-byte swizzle, the given box.
+int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t inner,
+                   uint64_t outer, uint64_t batch, uint64_t ld, uint64_t bstride, uint32_t box_inner,
+                   uint32_t box_outer);
+
+// Launch accounting / optional per-launch timing. Kinds group the library's
+// kernels for the profile read-out (lsr_profile_read).
+enum ProfKind : int {
+  PK_GEMM_GRAM = 0,     // NS phase 1: A = X X^T
+  PK_GEMM_POLY = 1,     // NS phase 2: B = bA + cA^2
+  PK_GEMM_UPDATE = 2,   // NS phase 3: X = aX + BX
+  PK_EW_ORIENT = 3,     // momentum / orientation / sum of squares
+  PK_EW_NORMALIZE = 4,  // norm finalize + scale
+  PK_EW_APPLY = 5,      // parameter update
+  PK_GEMM_OTHER = 6,    // plain GEMM / Gram / Kronecker / SOAP
+  PK_EW_OTHER = 7,      // other elementwise
+  PK_COUNT = 8
+};
+void count_launch();
+// Records a CUDA event on `st` before (begin) and after (end) a launch when
+// profiling is enabled; no-ops otherwise.
+void prof_begin(int kind, cudaStream_t st);
+void prof_end(int kind, cudaStream_t st);
+
+struct ProfScope {
+  int kind;
+  cudaStream_t st;
+  ProfScope(int k, cudaStream_t s) : kind(k), st(s) {
+    count_launch();
+    prof_begin(kind, st);
+  }
+  ~ProfScope() { prof_end(kind, st); }
+};
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+inline int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+// A GEMM operand as stored in memory: `batch` matrices of rows x cols
+// (row-major, row stride ld, batch stride bs, in elements). For operand A
+// (M x K) K-major means stored [M][K]; MN-major means stored [K][M]. Likewise
+// for operand B (N x K).
+struct Operand {
+  const void* base;
+  int rows, cols, ld;
+  long long bs;
+  int batch;
+  int mn;
+};
+
+// Tensor map for operand A (is_b = false, box rows BM) or B (box rows BN).
+inline int make_operand_map(CUtensorMap* map, const Operand& o, bool is_b, int BN) {
+  const uint32_t box_outer = o.mn ? 64u : static_cast<uint32_t>(is_b ? BN : BM);
+  return encode_tmap_3d(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, o.base, (uint64_t)o.cols, (uint64_t)o.rows,
+                        (uint64_t)std::max(o.batch, 1), (uint64_t)o.ld,
+                        (uint64_t)std::max<long long>(o.bs, (long long)o.rows * o.ld), 64u, box_outer);
+}
+
+// Fill tile counts and the flat tile numbering of every group.
+template <int BN>
+inline void finalize_tiles(GemmParams& p) {
+  int t = 0;
+  for (int g = 0; g < p.ngroups; ++g) {
+    GroupDesc& G = p.g[g];
+    G.tiles_m = cdiv(G.M, BM);
+    G.tiles_n = cdiv(G.N, BN);
+    if (!G.tri) {
+      G.tiles_per_mat = G.tiles_m * G.tiles_n;
+    } else {
+      int c = 0;
+      for (int ti = 0; ti < G.tiles_m; ++ti) c += std::max(0, G.tiles_n - tri_first_col_tile<BN>(ti));
+      G.tiles_per_mat = c;
+    }
+    G.tile_begin = t;
+    t += G.tiles_per_mat * G.batch;
+  }
+  p.total_tiles = t;
+}
+
+template <int BN, int STAGES, int EPI>
+inline int launch_gemm(GemmParams& p, cudaStream_t st, int kind = PK_GEMM_OTHER) {
+  using L = GemmSmem<BN, STAGES>;
+  static_assert(L::TOTAL <= 232448, "shared memory budget exceeded");
+  finalize_tiles<BN>(p);
+  if (p.total_tiles == 0) return LSR_OK;
+  p.status = status_ptr();
+  if (!p.status) return LSR_ERR_LAUNCH;
+  auto kfn = gemm_sm100_kernel<BN, STAGES, EPI>;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL) != cudaSuccess)
+    return LSR_ERR_LAUNCH;
+  const int grid = std::min(device_sm_count(), p.total_tiles);
+  ProfScope prof(kind, st);
+  kfn<<<grid, kGemmThreads, L::TOTAL, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? LSR_OK : LSR_ERR_LAUNCH;
+}
+
+}  // namespace lsr

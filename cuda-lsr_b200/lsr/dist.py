@@ -1,0 +1,146 @@
+"""ZeRO-1-style sharded Muon across the GPUs of one node.
+
+Ownership (the distribution of shard_groups): within each group of equally
+shaped matrices, matrix j is owned by rank j % world (round-robin, so every
+rank owns an equal, flop-balanced share when the group count divides by the
+world size; otherwise the last slots are padding). Each rank keeps the
+momentum of its own matrices only (ZeRO-1 optimizer-state sharding), runs the
+momentum update and Newton–Schulz for them, and the oriented bf16 updates of
+each group are all-gathered with NCCL on a communication stream while the next
+group is orthogonalised on the compute stream; every rank then applies all
+updates to its full parameter copy.
+
+The reference replicates Muon on every DDP rank (muon_lm_ddp.py:615-683); this
+module is the sharded replacement. Its host logic (ownership, gather order,
+padding) is independent of the CUDA engine, which is injectable for CPU tests.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+
+from .muon import NS_A, NS_B, NS_C, MuonStepEngine, adjusted_muon_lr
+
+
+def owner_of(j: int, world: int) -> int:
+    return j % world
+
+
+def local_count(count: int, world: int) -> int:
+    """Slots per rank for a group of `count` matrices (ceil; padding when uneven)."""
+    return (count + world - 1) // world
+
+
+def gathered_order(count: int, world: int) -> list[int | None]:
+    """Matrix index held by each slot of the rank-major all-gather buffer (None = padding)."""
+    per = local_count(count, world)
+    order: list[int | None] = []
+    for r in range(world):
+        for k in range(per):
+            j = k * world + r
+            order.append(j if j < count else None)
+    return order
+
+
+@dataclass
+class ShardGroup:
+    shape: tuple
+    lr: float
+    params: list            # all matrices of the group, in model order
+    owned: list = field(default_factory=list)  # indices j owned by this rank
+    momentum: list = field(default_factory=list)  # momentum buffers of the owned matrices
+    local_buf: torch.Tensor | None = None   # [per, m, n] oriented updates of this rank
+    gather_buf: torch.Tensor | None = None  # [world * per, m, n]
+
+
+class ShardedMuon:
+    """Muon step sharded over the ranks of `group` (default: the world).
+
+    params: list of 2-D bf16 CUDA parameters (all ranks pass the same list in
+    the same order). Gradients are read from ``p.grad`` of the owned matrices.
+    """
+
+    def __init__(self, params, lr=0.02, momentum=0.95, nesterov=True, weight_decay=0.01, ns_steps=5, eps=1e-7,
+                 lr_adjust="original", process_group=None, engine=None, overlap=True):
+        self.lr, self.mu, self.nesterov, self.wd = lr, momentum, nesterov, weight_decay
+        self.ns_steps, self.eps, self.lr_adjust = ns_steps, eps, lr_adjust
+        self.pg = process_group
+        self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(process_group) if dist.is_initialized() else 0
+        self.engine = engine if engine is not None else MuonStepEngine()
+        self.overlap = overlap
+        by_key: dict[tuple, ShardGroup] = {}
+        for p in params:
+            if p.ndim != 2:
+                raise ValueError("ShardedMuon only handles 2-D parameters")
+            key = (tuple(p.shape), adjusted_muon_lr(lr, p.shape, lr_adjust))
+            if key not in by_key:
+                by_key[key] = ShardGroup(shape=key[0], lr=key[1], params=[])
+            by_key[key].params.append(p)
+        self.groups = list(by_key.values())
+        for G in self.groups:
+            G.owned = [j for j in range(len(G.params)) if owner_of(j, self.world) == self.rank]
+            G.momentum = [torch.zeros_like(G.params[j]) for j in G.owned]
+            per = local_count(len(G.params), self.world)
+            m, n = min(G.shape), max(G.shape)
+            dev = G.params[0].device
+            G.local_buf = torch.zeros(per, m, n, dtype=torch.bfloat16, device=dev)
+            G.gather_buf = torch.zeros(self.world * per, m, n, dtype=torch.bfloat16, device=dev) \
+                if self.world > 1 else G.local_buf
+        self.comm_stream = torch.cuda.Stream() if (self.world > 1 and torch.cuda.is_available()) else None
+
+    def state_dict(self):
+        return {"momentum": [[b for b in G.momentum] for G in self.groups], "rank": self.rank, "world": self.world}
+
+    def load_state_dict(self, state):
+        if state["world"] != self.world or state["rank"] != self.rank:
+            raise ValueError("momentum shards were saved with a different world size / rank")
+        for G, bufs in zip(self.groups, state["momentum"]):
+            for dst, src in zip(G.momentum, bufs):
+                dst.copy_(src)
+
+    def _orthogonalize(self, G: ShardGroup) -> None:
+        items = [(G.params[j], G.params[j].grad, G.momentum[k], G.lr) for k, j in enumerate(G.owned)]
+        if any(it[1] is None for it in items):
+            raise RuntimeError("ShardedMuon: every owned parameter needs a gradient")
+        if not items:
+            return
+        grouped = [(G.shape, G.lr, items)]
+        self.engine.orthogonalize(grouped, momentum=self.mu, nesterov=self.nesterov, ns_steps=self.ns_steps,
+                                  eps=self.eps, coef=(NS_A, NS_B, NS_C), out=[G.local_buf[:len(items)]])
+
+    def _apply(self, G: ShardGroup) -> None:
+        order = gathered_order(len(G.params), self.world)
+        slots = [k for k, j in enumerate(order) if j is not None]
+        items = [(G.params[order[k]], None, None, G.lr) for k in slots]
+        if len(slots) == len(order):
+            upd = G.gather_buf
+        else:
+            upd = G.gather_buf[torch.tensor(slots, device=G.gather_buf.device)].contiguous()
+        self.engine.apply([(G.shape, G.lr, items)], [upd], weight_decay=self.wd, base_lr=self.lr)
+
+    @torch.no_grad()
+    def step(self) -> None:
+        if self.world == 1:
+            for G in self.groups:
+                self._orthogonalize(G)
+                self._apply(G)
+            return
+        compute = torch.cuda.current_stream()
+        comm = self.comm_stream
+        for G in self.groups:
+            self._orthogonalize(G)
+            if self.overlap:
+                ev = torch.cuda.Event()
+                ev.record(compute)
+                comm.wait_event(ev)
+                with torch.cuda.stream(comm):
+                    dist.all_gather_into_tensor(G.gather_buf, G.local_buf, group=self.pg)
+                    self._apply(G)
+            else:
+                dist.all_gather_into_tensor(G.gather_buf, G.local_buf, group=self.pg)
+                self._apply(G)
+        if self.overlap:
+            compute.wait_stream(comm)

@@ -1,0 +1,168 @@
+/*
+ * liblsr — C ABI of the B200 (sm_100a) optimizer hot path of cuda-lsr.
+ *
+ * Conventions shared by every entry point:
+ *   - pointers are device pointers unless a comment says "host";
+ *   - matrices are row-major with the given shape; batches are contiguous;
+ *   - all work is enqueued on `stream`; nothing synchronizes the host;
+ *   - nothing allocates: scratch memory comes from the caller's workspace
+ *     (`ws`, `ws_bytes`), sized by the matching *_workspace_bytes() query;
+ *   - the return value is LSR_OK or a negative LSR_ERR_* code; device-side
+ *     failures (a bounded wait that timed out) are recorded in the library's
+ *     device status word, read with lsr_device_status();
+ *   - calls are thread-safe as long as concurrent calls use distinct
+ *     workspaces.
+ *
+ * Each declaration names the reference interface it replaces (paths are
+ * relative to the cuda-lsr repository root).
+ */
+#ifndef LSR_H_
+#define LSR_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define LSR_API __attribute__((visibility("default")))
+#else
+#define LSR_API
+#endif
+
+typedef struct CUstream_st* lsr_stream_t; /* == cudaStream_t */
+
+#define LSR_OK 0
+#define LSR_ERR_ARG (-1)       /* null pointer, bad count or flag            */
+#define LSR_ERR_SHAPE (-2)     /* unsupported shape / batch / group count    */
+#define LSR_ERR_WORKSPACE (-3) /* workspace missing or too small             */
+#define LSR_ERR_LAUNCH (-4)    /* kernel launch failed (cudaGetLastError)    */
+#define LSR_ERR_DRIVER (-5)    /* TMA tensor-map encoding failed             */
+#define LSR_ERR_DEVICE (-6)    /* current device is not sm_100               */
+
+/* Library version string, e.g. "lsr-b200 0.1.0 (sm_100a)". */
+LSR_API const char* lsr_version(void);
+
+/* Human-readable message for an LSR_ERR_* code. */
+LSR_API const char* lsr_strerror(int code);
+
+/* Reads the device status word of the current device into *code (0 = no
+ * failure recorded) and clears it when `clear` is non-zero. Synchronizes the
+ * device. New: the reference has no device-side failure reporting. */
+LSR_API int lsr_device_status(int* code, int clear);
+
+/* Number of kernels this library has launched in this process. New: no
+ * counterpart in the reference (used to report launches per step). */
+LSR_API long long lsr_launch_count(void);
+
+/* Per-launch timing. While enabled, every kernel launch of the library is
+ * bracketed by two CUDA events recorded on its stream. lsr_profile_read
+ * waits for the recorded events and returns, per launch kind (0 = NS X X^T,
+ * 1 = NS b A + c A^2, 2 = NS a X + B X, 3 = momentum/orientation,
+ * 4 = normalisation, 5 = parameter update, 6 = other GEMMs, 7 = other
+ * elementwise), the summed milliseconds and launch counts, and clears the
+ * records when `reset` is non-zero. New: the reference times phases with
+ * torch CUDA events in its driver scripts (muon_lm_ddp.py:1309-1409). */
+LSR_API int lsr_profile_enable(int on);
+LSR_API int lsr_profile_read(double* ms, long long* launches, int nkinds, int reset);
+
+/* ------------------------------------------------------------------------
+ * Newton–Schulz quintic orthogonalisation (Muon).
+ *
+ * Replaces zeropower_serial(G, ns_steps, eps)           muon_lm_ddp.py:331-370
+ *      and zeropower_batched_oriented(X, ns_steps, eps) muon_lm_ddp.py:373-426
+ *
+ * in/out: bf16 [batch, rows, cols]. With orient=1 a tall input (rows > cols)
+ * is transposed before the iteration and the result transposed back
+ * (zeropower_serial); with orient=0 the polynomial runs on the input as
+ * given (zeropower_batched_oriented). Each matrix is divided by its bf16
+ * Frobenius norm clamped at eps, then `steps` times
+ *     A = X X^T ; B = b A + c A^2 ; X = a X + B X
+ * with bf16 storage between products and fp32 accumulation inside them,
+ * rounding at the same points as the reference's torch ops.
+ * `in` and `out` may not overlap the workspace; `out` may equal `in`.
+ * ---------------------------------------------------------------------- */
+LSR_API size_t lsr_ns_workspace_bytes(int batch, int rows, int cols, int orient);
+LSR_API int lsr_ns_bf16(const void* in, void* out, int batch, int rows, int cols, int orient, int steps, float a, float b,
+                float c, float eps, void* ws, size_t ws_bytes, lsr_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Muon step over groups of equally shaped parameter matrices.
+ *
+ * Replaces MuonAdamW._momentum_update   muon_lm_ddp.py:554-568
+ *          MuonAdamW._apply_update      muon_lm_ddp.py:571-593
+ *          MuonAdamW.muon_step_batched  muon_lm_ddp.py:615-683
+ *
+ * A group holds `count` bf16 matrices of shape rows x cols (unoriented
+ * parameter shape). grad_ptrs / mom_ptrs / param_ptrs are DEVICE arrays of
+ * `count` device addresses (uint64) of the gradients, momentum buffers and
+ * parameters. `lr` is the group's adjusted learning rate (adjusted_muon_lr).
+ * ---------------------------------------------------------------------- */
+typedef struct lsr_muon_group {
+  int rows;
+  int cols;
+  int count;
+  const uint64_t* grad_ptrs;
+  const uint64_t* mom_ptrs;
+  const uint64_t* param_ptrs;
+  float lr;
+} lsr_muon_group;
+
+/* Workspace for lsr_muon_step_bf16 / lsr_muon_orthogonalize_bf16 (host array
+ * of `ngroups` group descriptors). */
+LSR_API size_t lsr_muon_workspace_bytes(const lsr_muon_group* groups, int ngroups);
+
+/* Full step: momentum (and Nesterov) update, Newton–Schulz on every matrix,
+ * decoupled weight decay p *= 1 - base_lr*wd, then p -= lr * update. */
+LSR_API int lsr_muon_step_bf16(const lsr_muon_group* groups, int ngroups, float momentum, int nesterov,
+                       float weight_decay, float base_lr, int ns_steps, float a, float b, float c, float eps,
+                       void* ws, size_t ws_bytes, lsr_stream_t stream);
+
+/* Sharded step, part 1: momentum update and Newton–Schulz for the matrices of
+ * `groups`; group g's orthogonalised updates are written, oriented
+ * (min(rows,cols) x max(rows,cols)), into the bf16 buffer updates[g]
+ * [count, m, n] (host array of device pointers). */
+LSR_API int lsr_muon_orthogonalize_bf16(const lsr_muon_group* groups, int ngroups, float momentum, int nesterov,
+                                int ns_steps, float a, float b, float c, float eps, void* const* updates,
+                                void* ws, size_t ws_bytes, lsr_stream_t stream);
+
+/* Sharded step, part 2: apply oriented updates (e.g. after an all-gather) to
+ * the parameters of `groups` (grad/mom pointers are not read). */
+LSR_API int lsr_muon_apply_bf16(const lsr_muon_group* groups, int ngroups, const void* const* updates,
+                        float weight_decay, float base_lr, lsr_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Batched GEMM on the tcgen05 engine: D[b] = alpha * opA(A[b]) * opB(B[b]).
+ *
+ * Replaces the torch matmuls of the optimizer path (muon_lm_ddp.py:406-424,
+ * hft.py:127-138, shampoo.py:331-339).
+ *
+ * A is M x K stored [M][K] (a_trans=0) or [K][M] (a_trans=1); B is K x N
+ * stored [K][N] (b_trans=0) or [N][K] (b_trans=1); D is [M][N], bf16
+ * (out_f32=0) or fp32 (out_f32=1). Inputs bf16, fp32 accumulation. Every
+ * stored row length must be a multiple of 8 elements (16-byte TMA strides).
+ * ---------------------------------------------------------------------- */
+LSR_API int lsr_gemm_bf16(const void* A, const void* B, void* D, int batch, int M, int N, int K, int a_trans,
+                          int b_trans, int out_f32, float alpha, lsr_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Shampoo statistics update (symmetric Gram matrix, fp32, EMA):
+ *   side 0:  S[b] = beta * S[b] + alpha * G[b] G[b]^T    (S is rows x rows)
+ *   side 1:  S[b] = beta * S[b] + alpha * G[b]^T G[b]    (S is cols x cols)
+ *
+ * Replaces the L/R statistics update of DistributedShampoo (third-party
+ * distributed_shampoo, called from shampoo_soap_lm_ddp_zero1.py:609);
+ * config 3's  L = G_s G_s^T  is side 0 with beta = 0, alpha = 1.
+ * G is bf16 [batch, rows, cols] (cols a multiple of 8). Only the upper
+ * triangle is computed; the lower triangle is written as its mirror.
+ * ---------------------------------------------------------------------- */
+LSR_API int lsr_gram_update_f32(const void* G, void* S, int batch, int rows, int cols, int side, float beta,
+                                float alpha, lsr_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LSR_H_ */
