@@ -1,0 +1,411 @@
+#!/usr/bin/env python
+"""Benchmark: full GPT-2-XL Muon optimizer step on 1..8 B200 GPUs.
+
+Workload (the reference's headline Muon step, muon_lm_ddp.py:615-696, on its
+GPT-2-XL parameter set gpt2xl_4gpu_*.json:26-73): 48 layers x {1600x4800,
+1600x1600, 1600x6400, 6400x1600} = 192 bf16 matrices (1.4746 B parameters).
+One step = Nesterov momentum update + 5-step quintic Newton–Schulz of every
+matrix + decoupled weight decay and the lr-adjusted update (lr 0.02, wd 0.01,
+momentum 0.95, "original" lr adjust). Gradients / momentum N(0, 0.01^2) and
+parameters N(0, 0.02^2), bf16, seeded (seed 4) on the device.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl lsr|reference]
+
+N > 1 is launched with torch.distributed.run: the matrices of each shape group
+are sharded round-robin over the ranks (ZeRO-1), the orthogonalised updates are
+all-gathered with NCCL and applied on every rank (total work fixed: strong
+scaling). ``--impl reference`` times the CPU restatement of the reference path
+(the oracle; the reference itself is Python/torch) on the host cores, on a
+bounded sample extrapolated to the full step.
+
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "cuda-lsr_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+LAYER_SHAPES = [(1600, 4800), (1600, 1600), (1600, 6400), (6400, 1600)]  # c_attn, attn.c_proj, mlp.c_fc, mlp.c_proj
+N_LAYERS = 48
+NS_STEPS = 5
+LR, MU, WD, EPS = 0.02, 0.95, 0.01, 1e-7
+METRIC = "GPT-2-XL Muon optimizer step ms at 1/2/4/8 B200; % of dense bf16 TC peak"
+BASELINE_MS = 369.40  # gpt2xl_4gpu_batched.json:20 (4x RTX PRO 6000, Muon replicated)
+WORKLOAD = ("gpt2-xl muon step: 192 bf16 matrices (48 x {1600x4800, 1600x1600, 1600x6400, 6400x1600}), "
+            "nesterov momentum 0.95 + 5 Newton-Schulz steps + apply (lr 0.02, wd 0.01)")
+
+
+def ns_dense_flops(shape, steps=NS_STEPS) -> float:
+    m, n = min(shape), max(shape)
+    return steps * (4.0 * m * m * n + 2.0 * m ** 3)
+
+
+def phase_flops(shapes) -> dict:
+    """Dense (algorithmic) flops of one launch of each NS phase over all matrices."""
+    out = {"ns_gram": 0.0, "ns_poly": 0.0, "ns_update": 0.0}
+    for s in shapes:
+        m, n = min(s), max(s)
+        out["ns_gram"] += 2.0 * m * m * n
+        out["ns_poly"] += 2.0 * m ** 3
+        out["ns_update"] += 2.0 * m * m * n
+    return out
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return {"bf16_tflops": d["bf16_tflops"], "bf16_tflops_sustained": d["bf16_tflops_sustained"],
+                    "hbm_gbs": d["hbm_gbs"], "source": "measured"}
+        except Exception:
+            pass
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self._t:
+            self._t.join(timeout=2)
+        sm, mx, pw, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+                pw.append(float(f[3]))
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(pw) if pw else None, "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def physical_gpu(local_rank: int) -> int:
+    cvd = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if cvd:
+        toks = [t.strip() for t in cvd.split(",") if t.strip()]
+        if local_rank < len(toks) and toks[local_rank].isdigit():
+            return int(toks[local_rank])
+    return local_rank
+
+
+# ---------------------------------------------------------------------------
+# CPU side: oracle restatement of the reference path (bounded sample)
+# ---------------------------------------------------------------------------
+
+def cpu_layer_step_ms(seed: int = 4) -> float:
+    """Time one layer's Muon step (4 matrices) through the numpy oracle; returns ms."""
+    from oracle import muon as om
+    from oracle.bf16 import round_bf16
+    rng = np.random.default_rng(seed)
+    P = [round_bf16(rng.standard_normal(s, dtype=np.float32) * 0.02) for s in LAYER_SHAPES]
+    G = [round_bf16(rng.standard_normal(s, dtype=np.float32) * 0.01) for s in LAYER_SHAPES]
+    M = [round_bf16(rng.standard_normal(s, dtype=np.float32) * 0.01) for s in LAYER_SHAPES]
+    t0 = time.perf_counter()
+    om.muon_step(P, G, M, lr=LR, mu=MU, nesterov=True, wd=WD, ns_steps=NS_STEPS, eps=EPS)
+    return (time.perf_counter() - t0) * 1e3
+
+
+def run_reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_layer_step_ms()
+    samples = [cpu_layer_step_ms() for _ in range(args.steps)]
+    layer_ms = statistics.median(samples)
+    value = layer_ms * N_LAYERS
+    sample = (f"1 of 48 layers (4 matrices 1600x4800, 1600x1600, 1600x6400, 6400x1600), full Muon step "
+              f"(momentum, 5 NS steps, apply) through the numpy restatement, x48; median of {args.steps}")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "ms", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 3), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": round(value / BASELINE_MS, 4), "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.01^2) grads/momentum, N(0,0.02^2) params)",
+        "config": {"workload": WORKLOAD, "parallelism": "host cores", "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "ms", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU side
+# ---------------------------------------------------------------------------
+
+def make_params(device, layers: int):
+    g = torch.Generator(device=device).manual_seed(4)
+    shapes = [s for _ in range(layers) for s in LAYER_SHAPES]
+    P = [(torch.randn(s, generator=g, device=device) * 0.02).bfloat16() for s in shapes]
+    G = [(torch.randn(s, generator=g, device=device) * 0.01).bfloat16() for s in shapes]
+    M = [(torch.randn(s, generator=g, device=device) * 0.01).bfloat16() for s in shapes]
+    return shapes, P, G, M
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def run_lsr(args) -> None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    import lsr
+    from lsr import _lib
+    from lsr.dist import ShardedMuon
+
+    shapes, P, G, M = make_params(dev, args.layers)
+    params = [torch.nn.Parameter(p) for p in P]
+    named = [(f"h.{i // 4}.w{i % 4}", p) for i, p in enumerate(params)]
+
+    if world == 1:
+        opt = lsr.MuonAdamW(named, muon_mode="batched", muon_lr=LR, muon_momentum=MU, muon_weight_decay=WD,
+                            muon_nesterov=True, muon_ns_steps=NS_STEPS, muon_eps=EPS, muon_lr_adjust="original",
+                            muon_batch_matrices=8, adam_lr=3e-4, adam_betas=(0.9, 0.95), adam_weight_decay=0.0,
+                            rank=0)
+        for p, m in zip(params, M):
+            opt.momentum[p].copy_(m)
+        step = opt.muon_step
+    else:
+        opt = ShardedMuon(params, lr=LR, momentum=MU, nesterov=True, weight_decay=WD, ns_steps=NS_STEPS, eps=EPS)
+        for Gp in opt.groups:
+            for k, j in enumerate(Gp.owned):
+                idx = next(i for i, p in enumerate(params) if p is Gp.params[j])
+                Gp.momentum[k].copy_(M[idx])
+        step = opt.step
+    for p, gr in zip(params, G):
+        p.grad = gr
+    del M
+
+    # ---------------------------------------------------------------- device-timed
+    for _ in range(args.warmup):
+        step()
+    barrier(world)
+    sampler = ClockSampler(physical_gpu(local_rank))
+    sampler.start()
+    time.sleep(0.3)
+    _lib.profile_enable(True)
+    _lib.profile_read(reset=True)
+    launches0 = _lib.launch_count()
+    barrier(world)
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for _ in range(args.steps):
+        step()
+    t_end.record()
+    barrier(world)
+    launches = _lib.launch_count() - launches0
+    _lib.profile_enable(False)
+    prof = _lib.profile_read(reset=True)
+    clocks = sampler.stop()
+    ms = t_start.elapsed_time(t_end) / args.steps
+    ms = max_over_ranks(ms, world)
+
+    peaks = measured_peaks()
+    # dominant kernel: the NS launch kind with the largest total time
+    ns_kinds = ("ns_gram", "ns_poly", "ns_update")
+    dom = max(ns_kinds, key=lambda k: prof[k][0])
+    dom_ms, dom_n = prof[dom]
+    my_shapes = shapes if world == 1 else [opt.groups[gi].shape for gi in range(len(opt.groups))
+                                           for _ in opt.groups[gi].owned]
+    per_launch_flops = phase_flops(my_shapes)[dom]
+    if world == 1:
+        # one launch per NS step covers every group (<= 4 groups per launch)
+        launches_per_step = NS_STEPS * ((len(set(shapes)) + 3) // 4)
+        flops_per_launch = per_launch_flops / (launches_per_step // NS_STEPS)
+    else:
+        flops_per_launch = per_launch_flops / len(opt.groups)  # one launch per group per NS step
+    dom_avg_ms = dom_ms / max(dom_n, 1)
+    achieved = flops_per_launch / (dom_avg_ms * 1e-3) / 1e12 if dom_n else None
+    step_flops = sum(ns_dense_flops(s) for s in shapes)
+    traffic = load_traffic(dom)
+    roofline = {
+        "bound": "tensor", "kernel": f"gemm_sm100_kernel ({dom})",
+        "achieved": round(achieved, 1) if achieved else None,
+        "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+        "frac": round(achieved / peaks["bf16_tflops_sustained"], 4) if achieved else None,
+        "peak_kind": f"bf16_tflops_sustained ({peaks['source']})",
+        "traffic": traffic,
+        "dense_flops_per_launch": flops_per_launch, "avg_launch_ms": round(dom_avg_ms, 4),
+        "step": {"dense_tflop": round(step_flops / 1e12, 3),
+                 "achieved_tflops": round(step_flops / (ms * 1e-3) / 1e12, 1),
+                 "frac_of_sustained": round(step_flops / (ms * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"], 4),
+                 "frac_of_burst": round(step_flops / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4)},
+        "per_kind_ms_per_step": {k: round(v[0] / args.steps, 3) for k, v in prof.items() if v[1]},
+    }
+
+    # ---------------------------------------------------------------- end to end (host buffers)
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, params, G, step, world, opt)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        layer_ms = statistics.median([cpu_layer_step_ms() for _ in range(2)])
+        cpu = {"value": round(layer_ms * N_LAYERS, 1), "unit": "ms", "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": "1 of 48 layers (4 matrices), full Muon step via the numpy restatement, x48; median of 2"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(ms, 3), "unit": "ms", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": round(ms / BASELINE_MS, 4), "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.01^2) grads/momentum, N(0,0.02^2) params, generated on device)",
+            "config": {"workload": WORKLOAD, "layers": args.layers, "ns_steps": NS_STEPS,
+                       "parallelism": "single gpu" if world == 1 else f"zero1 round-robin shards x{world}",
+                       "l2": "inputs larger than L2 (8.8 GB params+grads+momentum)"},
+            "roofline": roofline, "clocks": clocks, "gpu_launches": int(launches), "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(args, params, grads, step, world, opt):
+    """Same step through the public API with host buffers: pinned grads -> device,
+    step, updated parameters -> pinned host, inside the timed region."""
+    if world == 1:
+        need = list(range(len(params)))
+    else:
+        need = sorted({next(i for i, p in enumerate(params) if p is Gp.params[j]) for Gp in opt.groups
+                       for j in Gp.owned})
+    host_g = {i: torch.empty(grads[i].shape, dtype=torch.bfloat16, pin_memory=True) for i in need}
+    for i in need:
+        host_g[i].copy_(grads[i])
+    host_p = [torch.empty(p.shape, dtype=torch.bfloat16, pin_memory=True) for p in params]
+    h2d = sum(host_g[i].numel() * 2 for i in need)
+    d2h = sum(h.numel() * 2 for h in host_p)
+
+    def e2e_step():
+        for i in need:
+            params[i].grad.copy_(host_g[i], non_blocking=True)
+        step()
+        for p, h in zip(params, host_p):
+            h.copy_(p.data, non_blocking=True)
+
+    for _ in range(max(1, min(args.warmup, 2))):
+        e2e_step()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = max(1, min(args.steps, 5))
+    a.record()
+    for _ in range(n):
+        e2e_step()
+    b.record()
+    barrier(world)
+    ms = max_over_ranks(a.elapsed_time(b) / n, world)
+    return {"value": round(ms, 3), "unit": "ms", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "steps": n, "path": "lsr.MuonAdamW.muon_step" if world == 1 else "lsr.dist.ShardedMuon.step"}
+
+
+def load_traffic(kind: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if present."""
+    f = ROOT / "profiles" / "traffic.json"
+    if not f.exists():
+        return None
+    try:
+        return json.loads(f.read_text()).get(kind)
+    except Exception:
+        return None
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["lsr", "reference"], default="lsr")
+    ap.add_argument("--layers", type=int, default=N_LAYERS, help="GPT-2-XL layers (48 = the full model)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return 0
+    run_lsr(args)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -5,7 +5,6 @@
 namespace lsr {
 namespace {
 constexpr int G_BN = 256;
-constexpr int G_STAGES = 4;
 }  // namespace
 }  // namespace lsr
 
@@ -38,7 +37,7 @@ int lsr_gemm_bf16(const void* A, const void* B, void* D, int batch, int M, int N
   G.ldo = N;
   G.alpha = alpha;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  return out_f32 ? launch_gemm<G_BN, G_STAGES, EPI_STORE_F32>(p, st) : launch_gemm<G_BN, G_STAGES, EPI_STORE_BF16>(p, st);
+  return out_f32 ? launch_gemm<G_BN, EPI_STORE_F32>(p, st) : launch_gemm<G_BN, EPI_STORE_BF16>(p, st);
 }
 
 int lsr_gram_update_f32(const void* Gm, void* S, int batch, int rows, int cols, int side, float beta, float alpha,
@@ -66,9 +65,12 @@ int lsr_gram_update_f32(const void* Gm, void* S, int batch, int rows, int cols, 
   G.out = S;
   G.out_bs = (long long)n * n;
   G.ldo = n;
+  G.aux = S;  // the old statistic, read by the EMA epilogue
+  G.aux_bs = (long long)n * n;
+  G.ld_aux = n;
   G.alpha = alpha;
   G.beta = beta;
-  return launch_gemm<G_BN, G_STAGES, EPI_F32_EMA>(p, reinterpret_cast<cudaStream_t>(stream));
+  return launch_gemm<G_BN, EPI_F32_EMA>(p, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -63,11 +63,13 @@ struct GroupDesc {
   long long aux_bs;
   int ld_aux;
   float alpha, beta;
+  int tma_out;  // epilogue stages 32x32 chunks in smem and stores them with TMA (mapOut)
 };
 
 struct GemmParams {
   CUtensorMap mapA[kMaxGroups][kMaxSeg];
   CUtensorMap mapB[kMaxGroups][kMaxSeg];
+  CUtensorMap mapOut[kMaxGroups];  // output in stored orientation, box 32 x 32
   GroupDesc g[kMaxGroups];
   int ngroups;
   int total_tiles;
@@ -232,23 +234,185 @@ __device__ __forceinline__ void epilogue_chunk(const GroupDesc& G, int b, int ro
 }
 
 // ---------------------------------------------------------------------------
+// Staged epilogue: each epilogue warp owns 32 rows of the tile and walks the
+// tile's 32-column chunks. Per chunk:
+//   * the aux operand (A for POLY, X for UPDATE, the old statistic for EMA) is
+//     read with coalesced 16-byte loads one chunk ahead, written into a
+//     swizzled 32x32 smem staging buffer, and each thread reads back its row;
+//   * results go back into the same buffer (own row only) and, for mirrored /
+//     transposed outputs, column-wise into a second buffer;
+//   * one lane stores the buffer(s) with TMA (OOB rows/cols are clipped).
+// Staging rows are 64 B (bf16) or 128 B (fp32), laid out with the TMA 64B /
+// 128B swizzle so thread-per-row accesses are conflict-free.
+// ---------------------------------------------------------------------------
+
+template <int EPI>
+struct EpiT {
+  static constexpr bool F32 = (EPI == EPI_STORE_F32 || EPI == EPI_F32_EMA);
+  static constexpr int ESZ = F32 ? 4 : 2;
+  static constexpr int ROWB = 32 * ESZ;  // bytes per staged row
+  static constexpr int CHB = 32 * ROWB;  // bytes per staged 32x32 chunk
+  static constexpr int VPR = ROWB / 16;  // 16-byte vectors per staged row
+  static constexpr int EPV = 16 / ESZ;   // elements per 16-byte vector
+  static constexpr bool AUX = (EPI == EPI_NS_POLY || EPI == EPI_NS_UPDATE || EPI == EPI_F32_EMA);
+};
+
+template <int ROWB>
+__device__ __forceinline__ uint32_t stg_off(int r, int j) {
+  if constexpr (ROWB == 64)
+    return (uint32_t)(r * 64 + 16 * (j ^ ((r >> 1) & 3)));
+  else
+    return (uint32_t)(r * 128 + 16 * (j ^ (r & 7)));
+}
+
+// Coalesced load of the aux chunk (32 rows x 32 cols at row0/col0) into
+// registers: lane l holds vectors l + 32 i (row = idx / VPR, vector = idx % VPR).
+template <int EPI>
+__device__ __forceinline__ void aux_prefetch(const GroupDesc& G, int b, int row0, int col0, int lane,
+                                             uint4 (&pre)[EpiT<EPI>::VPR]) {
+  using T = EpiT<EPI>;
+  const uint8_t* base = reinterpret_cast<const uint8_t*>(G.aux) + (long long)b * G.aux_bs * T::ESZ;
+#pragma unroll
+  for (int i = 0; i < T::VPR; ++i) {
+    const int idx = lane + 32 * i;
+    const int r = idx / T::VPR, j = idx % T::VPR;
+    const int gr = row0 + r, gc = col0 + j * T::EPV;
+    if (gr < G.M && gc < G.N)
+      pre[i] = __ldg(reinterpret_cast<const uint4*>(base + ((long long)gr * G.ld_aux + gc) * T::ESZ));
+    else
+      pre[i] = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk_staged(const GemmParams& p, int g, const GroupDesc& G, int b,
+                                                      int row0, int col0, int lane, const uint32_t (&r)[32],
+                                                      const uint4 (&cur)[EpiT<EPI>::VPR], uint8_t* dbuf,
+                                                      uint8_t* tbuf) {
+  using T = EpiT<EPI>;
+  // buffers of chunk k-2 must have been read by their TMA store
+  if (lane == 0) bulk_wait_read<1>();
+  __syncwarp();
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  if constexpr (T::AUX) {
+#pragma unroll
+    for (int i = 0; i < T::VPR; ++i) {
+      const int idx = lane + 32 * i;
+      *reinterpret_cast<uint4*>(dbuf + stg_off<T::ROWB>(idx / T::VPR, idx % T::VPR)) = cur[i];
+    }
+    __syncwarp();
+    float x[32];
+#pragma unroll
+    for (int j = 0; j < T::VPR; ++j) {
+      const uint4 u = *reinterpret_cast<const uint4*>(dbuf + stg_off<T::ROWB>(lane, j));
+      if constexpr (T::F32) {
+        x[4 * j] = __uint_as_float(u.x);
+        x[4 * j + 1] = __uint_as_float(u.y);
+        x[4 * j + 2] = __uint_as_float(u.z);
+        x[4 * j + 3] = __uint_as_float(u.w);
+      } else {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          x[8 * j + 2 * e] = f.x;
+          x[8 * j + 2 * e + 1] = f.y;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if constexpr (EPI == EPI_NS_POLY)
+        v[j] = bf16r(G.alpha * x[j]) + bf16r(G.beta * bf16r(v[j]));
+      else if constexpr (EPI == EPI_NS_UPDATE)
+        v[j] = bf16r(G.alpha * x[j]) + bf16r(v[j]);
+      else  // EMA
+        v[j] = (G.beta != 0.f) ? fmaf(G.beta, x[j], G.alpha * v[j]) : G.alpha * v[j];
+    }
+  } else if constexpr (EPI == EPI_STORE_BF16 || EPI == EPI_STORE_F32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = G.alpha * v[j];
+  }
+  const bool diag = G.tri && col0 == row0;
+  const bool direct = !G.out_trans;
+  const bool transposed = G.out_trans || (G.tri && col0 > row0);
+  if (direct) {
+#pragma unroll
+    for (int j = 0; j < T::VPR; ++j) {
+      uint4 u;
+      if constexpr (T::F32) {
+        u = make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]), __float_as_uint(v[4 * j + 2]),
+                       __float_as_uint(v[4 * j + 3]));
+      } else {
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
+      }
+      *reinterpret_cast<uint4*>(dbuf + stg_off<T::ROWB>(lane, j)) = u;
+    }
+  }
+  if (diag) {
+    // symmetric diagonal block: overwrite the lower triangle with the mirror of the upper
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j > lane) {
+        uint8_t* dst = dbuf + stg_off<T::ROWB>(j, (lane * T::ESZ) / 16) + (lane * T::ESZ) % 16;
+        if constexpr (T::F32)
+          *reinterpret_cast<float*>(dst) = v[j];
+        else
+          *reinterpret_cast<__nv_bfloat16*>(dst) = __float2bfloat16_rn(v[j]);
+      }
+    }
+  } else if (transposed) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      uint8_t* dst = tbuf + stg_off<T::ROWB>(j, (lane * T::ESZ) / 16) + (lane * T::ESZ) % 16;
+      if constexpr (T::F32)
+        *reinterpret_cast<float*>(dst) = v[j];
+      else
+        *reinterpret_cast<__nv_bfloat16*>(dst) = __float2bfloat16_rn(v[j]);
+    }
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    const CUtensorMap* mo = &p.mapOut[g];
+    if (direct) tma_store_3d(mo, dbuf, col0, row0, b);
+    if (transposed && !diag) tma_store_3d(mo, tbuf, row0, col0, b);
+    bulk_commit();
+  }
+}
+
+// ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int EPI>
 struct GemmSmem {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int EPI_BYTES = (kEpiThreads / 32) * 4 * EpiT<EPI>::CHB;  // per warp: 2 direct + 2 transposed
+  static constexpr int BAR_OFFSET = EPI_OFFSET + EPI_BYTES;
   static constexpr int BAR_BYTES = 8 * (2 * STAGES + 5) + 16;
   static constexpr int TOTAL = BAR_OFFSET + BAR_BYTES + 1024;  // + alignment slack
 };
 
+// Pipeline depth that fits next to the epilogue staging buffers.
+template <int EPI>
+constexpr int default_stages() {
+  return EpiT<EPI>::F32 ? 3 : 4;
+}
+
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __grid_constant__ GemmParams p) {
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 64 in [64, 256]");
-  using L = GemmSmem<BN, STAGES>;
+  using L = GemmSmem<BN, STAGES, EPI>;
+  using ET = EpiT<EPI>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -403,34 +567,64 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    uint8_t* ebase = smem + L::EPI_OFFSET + (warp - 2) * 4 * ET::CHB;
     int acc = 0;
     uint32_t aph = 0;
+    uint32_t kchunk = 0;  // chunks processed by this warp (staging buffer parity)
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
       int g, b, ti, tj;
       decode_tile<BN>(p, t, g, b, ti, tj);
       const GroupDesc& G = p.g[g];
+      const int row0 = ti * BM + q * 32;  // first row of this warp
+      // warp-uniform mask of live 32-column chunks
+      uint32_t live = 0;
+      if (row0 < G.M) {
+#pragma unroll
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          const int col0 = tj * BN + cc * 32;
+          if (col0 < G.N && !(G.tri && col0 < row0)) live |= 1u << cc;
+        }
+      }
+      uint4 pre[ET::VPR];
+#pragma unroll
+      for (int i = 0; i < ET::VPR; ++i) pre[i] = make_uint4(0u, 0u, 0u, 0u);
+      if constexpr (ET::AUX) {
+        if (G.tma_out && live) aux_prefetch<EPI>(G, b, row0, tj * BN + (__ffs(live) - 1) * 32, lane, pre);
+      }
       if (!mbar_wait(tfull + acc, aph, abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
-      const int row0 = ti * BM + q * 32;  // first row of this warp
-      const int row = row0 + lane;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      const bool warp_rows_live = row0 < G.M;
-#pragma unroll 1
-      for (int cc = 0; cc < BN / 32; ++cc) {
+      uint32_t rem = live;
+      while (rem) {
+        const int cc = __ffs(rem) - 1;
+        rem &= rem - 1;
         const int col0 = tj * BN + cc * 32;
-        // warp-uniform skips: columns past N, or (triangle) chunk fully below the diagonal
-        if (!warp_rows_live || col0 >= G.N) continue;
-        if (G.tri && col0 + 31 < row0) continue;
         uint32_t r[32];
         tmem_ld32(tbase + static_cast<uint32_t>(cc * 32), r);
-        tmem_ld_wait();
-        epilogue_chunk<EPI>(G, b, row, col0, r);
+        if (G.tma_out) {
+          uint4 cur[ET::VPR];
+#pragma unroll
+          for (int i = 0; i < ET::VPR; ++i) cur[i] = pre[i];
+          if constexpr (ET::AUX) {
+            if (rem) aux_prefetch<EPI>(G, b, row0, tj * BN + (__ffs(rem) - 1) * 32, lane, pre);
+          }
+          tmem_ld_wait();
+          uint8_t* dbuf = ebase + (kchunk & 1) * ET::CHB;
+          uint8_t* tbuf = ebase + (2 + (kchunk & 1)) * ET::CHB;
+          epilogue_chunk_staged<EPI>(p, g, G, b, row0, col0, lane, r, cur, dbuf, tbuf);
+          ++kchunk;
+        } else {
+          tmem_ld_wait();
+          epilogue_chunk<EPI>(G, b, row0 + lane, col0, r);
+        }
       }
       tc_fence_before();
       mbar_arrive(tempty + acc);
       acc ^= 1;
       if (acc == 0) aph ^= 1;
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();

@@ -25,7 +25,6 @@ namespace {
 constexpr int TILE = 64;
 constexpr int EW_THREADS = 256;
 constexpr int NS_BN = 256;
-constexpr int NS_STAGES = 4;
 
 typedef __nv_bfloat16 bf16;
 
@@ -55,16 +54,65 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return t;  // valid in thread 0
 }
 
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 t = __bfloat1622float2(h[e]);
+    f[2 * e] = t.x;
+    f[2 * e + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 v;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
+  return v;
+}
+
+__device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// 64x64 bf16 tile in shared memory as 64 rows of 32 32-bit words. The word
+// index is XOR-swizzled by the row's 8-row group so that reading one column
+// for 8 rows 8 apart (the transposed read) hits distinct banks, while each
+// 16-byte vector (4 aligned words) of a row stays contiguous.
+__device__ __forceinline__ int swz(int row, int word) { return row * 32 + (word ^ (((row >> 3) & 7) << 2)); }
+
+__device__ __forceinline__ float tile_get(const uint32_t* t, int row, int col) {
+  const uint32_t w = t[swz(row, col >> 1)];
+  const uint16_t h = (col & 1) ? (uint16_t)(w >> 16) : (uint16_t)(w & 0xFFFFu);
+  return __bfloat162float(__ushort_as_bfloat16(h));
+}
+
+// Momentum / Nesterov on 8 elements (muon_lm_ddp.py:554-568 rounding order).
+template <bool MOMENTUM>
+__device__ __forceinline__ void momentum8(const float (&g)[8], float (&buf)[8], float (&u)[8], float mu,
+                                          int nesterov) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    if constexpr (MOMENTUM) {
+      buf[e] = bf16r(bf16r(mu * buf[e]) + g[e]);
+      u[e] = nesterov ? bf16r(g[e] + bf16r(mu * buf[e])) : buf[e];
+    } else {
+      u[e] = g[e];
+    }
+  }
+}
+
 // One block per 64x64 tile of the source matrix (R x C row-major, ld = C).
 //   MOMENTUM=false: u = src
 //   MOMENTUM=true : buf = bf16(bf16(mu*buf) + g); u = nesterov ? bf16(g + bf16(mu*buf)) : buf
 // u is written oriented into X (transposed when `trans`), and the tile's sum of
-// u^2 into partials[b * gridDim.x + tile].
+// u^2 into partials[b * gridDim.x + tile]. 16-byte vector path when the row
+// lengths are multiples of 8 and the matrices 16-byte aligned; scalar path
+// otherwise (ragged shapes).
 template <bool MOMENTUM>
 __global__ void __launch_bounds__(EW_THREADS) orient_kernel(MatRef src, MatRef mom, int R, int C, int trans, bf16* X,
                                                             long long x_bs, int ldx, float* partials, float mu,
                                                             int nesterov) {
-  __shared__ float tile[TILE][TILE + 1];
+  __shared__ __align__(16) float smem[TILE * (TILE + 1)];
   __shared__ float red[EW_THREADS / 32];
   const int b = blockIdx.y;
   const int tiles_c = (C + TILE - 1) / TILE;
@@ -73,45 +121,90 @@ __global__ void __launch_bounds__(EW_THREADS) orient_kernel(MatRef src, MatRef m
   const bf16* g = mat_at(src, b);
   bf16* buf = MOMENTUM ? mat_at(mom, b) : nullptr;
   bf16* xd = X + (long long)b * x_bs;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int tid = threadIdx.x;
   float ss = 0.f;
-#pragma unroll 2
-  for (int k = 0; k < TILE / 8; ++k) {
-    const int i = ty + 8 * k;
-    const int r = r0 + i;
+  const bool vec = (C % 8 == 0) && (!trans || R % 8 == 0) && (ldx % 8 == 0) && aligned16(g) && aligned16(xd) &&
+                   (!MOMENTUM || aligned16(buf));
+  if (vec) {
+    uint32_t* tile = reinterpret_cast<uint32_t*>(smem);
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int j = 2 * tx + e;
-      const int c = c0 + j;
-      float u = 0.f;
+    for (int k = 0; k < 2; ++k) {
+      const int i = (tid >> 3) + 32 * k;
+      const int v = tid & 7;
+      const int r = r0 + i, c = c0 + 8 * v;
+      float u[8];
       if (r < R && c < C) {
         const long long idx = (long long)r * C + c;
-        const float gv = __bfloat162float(g[idx]);
-        if constexpr (MOMENTUM) {
-          float bv = __bfloat162float(buf[idx]);
-          bv = bf16r(bf16r(mu * bv) + gv);
-          buf[idx] = __float2bfloat16_rn(bv);
-          u = nesterov ? bf16r(gv + bf16r(mu * bv)) : bv;
-        } else {
-          u = gv;
-        }
-        ss = fmaf(u, u, ss);
-        if (!trans) xd[(long long)r * ldx + c] = __float2bfloat16_rn(u);
+        float gf[8], bf[8];
+        unpack8(*reinterpret_cast<const uint4*>(g + idx), gf);
+        if constexpr (MOMENTUM) unpack8(*reinterpret_cast<const uint4*>(buf + idx), bf);
+        momentum8<MOMENTUM>(gf, bf, u, mu, nesterov);
+        if constexpr (MOMENTUM) *reinterpret_cast<uint4*>(buf + idx) = pack8(bf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = fmaf(u[e], u[e], ss);
+        if (!trans) *reinterpret_cast<uint4*>(xd + (long long)r * ldx + c) = pack8(u);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) u[e] = 0.f;
       }
-      tile[i][j] = u;
+      if (trans) *reinterpret_cast<uint4*>(&tile[swz(i, 4 * v)]) = pack8(u);
     }
-  }
-  if (trans) {
-    __syncthreads();
+    if (trans) {
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int cc = (tid >> 3) + 32 * k;  // source column offset = destination row offset
+        const int v = tid & 7;               // destination columns = source rows r0 + 8v .. +7
+        const int xr = c0 + cc, xc = r0 + 8 * v;
+        if (xr < C && xc < R) {
+          float f[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] = tile_get(tile, 8 * v + e, cc);
+          *reinterpret_cast<uint4*>(xd + (long long)xr * ldx + xc) = pack8(f);
+        }
+      }
+    }
+  } else {
+    float(*tile)[TILE + 1] = reinterpret_cast<float(*)[TILE + 1]>(smem);
+    const int tx = tid & 31, ty = tid >> 5;
 #pragma unroll 2
     for (int k = 0; k < TILE / 8; ++k) {
-      const int jj = ty + 8 * k;  // source column offset = destination row offset
-      const int dr = c0 + jj;
-      if (dr >= C) continue;
+      const int i = ty + 8 * k;
+      const int r = r0 + i;
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int ii = 2 * tx + e;  // source row offset = destination column offset
-        if (r0 + ii < R) xd[(long long)dr * ldx + (r0 + ii)] = __float2bfloat16_rn(tile[ii][jj]);
+        const int j = 2 * tx + e;
+        const int c = c0 + j;
+        float u = 0.f;
+        if (r < R && c < C) {
+          const long long idx = (long long)r * C + c;
+          const float gv = __bfloat162float(g[idx]);
+          if constexpr (MOMENTUM) {
+            float bv = __bfloat162float(buf[idx]);
+            bv = bf16r(bf16r(mu * bv) + gv);
+            buf[idx] = __float2bfloat16_rn(bv);
+            u = nesterov ? bf16r(gv + bf16r(mu * bv)) : bv;
+          } else {
+            u = gv;
+          }
+          ss = fmaf(u, u, ss);
+          if (!trans) xd[(long long)r * ldx + c] = __float2bfloat16_rn(u);
+        }
+        tile[i][j] = u;
+      }
+    }
+    if (trans) {
+      __syncthreads();
+#pragma unroll 2
+      for (int k = 0; k < TILE / 8; ++k) {
+        const int jj = ty + 8 * k;
+        const int dr = c0 + jj;
+        if (dr >= C) continue;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int ii = 2 * tx + e;
+          if (r0 + ii < R) xd[(long long)dr * ldx + (r0 + ii)] = __float2bfloat16_rn(tile[ii][jj]);
+        }
       }
     }
   }
@@ -139,7 +232,18 @@ __global__ void __launch_bounds__(EW_THREADS) scale_kernel(bf16* X, long long x_
   const int b = blockIdx.y;
   const float d = nrm[b];
   bf16* row = X + (long long)b * x_bs + (long long)blockIdx.x * ldx;
-  for (int j = threadIdx.x; j < n; j += blockDim.x) row[j] = __float2bfloat16_rn(__fdiv_rn(__bfloat162float(row[j]), d));
+  if ((n % 8 == 0) && aligned16(row)) {
+    for (int j = 8 * threadIdx.x; j < n; j += 8 * blockDim.x) {
+      float f[8];
+      unpack8(*reinterpret_cast<const uint4*>(row + j), f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = __fdiv_rn(f[e], d);
+      *reinterpret_cast<uint4*>(row + j) = pack8(f);
+    }
+  } else {
+    for (int j = threadIdx.x; j < n; j += blockDim.x)
+      row[j] = __float2bfloat16_rn(__fdiv_rn(__bfloat162float(row[j]), d));
+  }
 }
 
 // One block per 64x64 tile of the parameter matrix (R x C). U holds the
@@ -149,14 +253,56 @@ __global__ void __launch_bounds__(EW_THREADS) scale_kernel(bf16* X, long long x_
 __global__ void __launch_bounds__(EW_THREADS) apply_kernel(MatRef param, int R, int C, int trans, const bf16* U,
                                                            long long u_bs, int ldu, float wd_factor, int apply_wd,
                                                            float neg_lr) {
-  __shared__ float tile[TILE][TILE + 1];
+  __shared__ __align__(16) float smem[TILE * (TILE + 1)];
   const int b = blockIdx.y;
   const int tiles_c = (C + TILE - 1) / TILE;
   const int r0 = (blockIdx.x / tiles_c) * TILE;
   const int c0 = (blockIdx.x % tiles_c) * TILE;
   bf16* p = mat_at(param, b);
   const bf16* u = U + (long long)b * u_bs;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int tid = threadIdx.x;
+  const bool vec = (C % 8 == 0) && (!trans || R % 8 == 0) && (ldu % 8 == 0) && aligned16(p) && aligned16(u);
+  if (vec) {
+    uint32_t* tile = reinterpret_cast<uint32_t*>(smem);
+    if (trans) {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int uu = (tid >> 3) + 32 * k;  // U row offset = parameter column offset
+        const int v = tid & 7;               // U columns = parameter rows r0 + 8v .. +7
+        const int ur = c0 + uu, uc = r0 + 8 * v;
+        uint4 val = make_uint4(0u, 0u, 0u, 0u);
+        if (ur < C && uc < R) val = *reinterpret_cast<const uint4*>(u + (long long)ur * ldu + uc);
+        *reinterpret_cast<uint4*>(&tile[swz(uu, 4 * v)]) = val;
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = (tid >> 3) + 32 * k;
+      const int v = tid & 7;
+      const int r = r0 + i, c = c0 + 8 * v;
+      if (r >= R || c >= C) continue;
+      float uf[8], pf[8];
+      if (trans) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) uf[e] = tile_get(tile, 8 * v + e, i);
+      } else {
+        unpack8(*reinterpret_cast<const uint4*>(u + (long long)r * ldu + c), uf);
+      }
+      const long long idx = (long long)r * C + c;
+      unpack8(*reinterpret_cast<const uint4*>(p + idx), pf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float pv = pf[e];
+        if (apply_wd) pv = bf16r(pv * wd_factor);
+        pf[e] = fmaf(neg_lr, uf[e], pv);
+      }
+      *reinterpret_cast<uint4*>(p + idx) = pack8(pf);
+    }
+    return;
+  }
+  float(*tile)[TILE + 1] = reinterpret_cast<float(*)[TILE + 1]>(smem);
+  const int tx = tid & 31, ty = tid >> 5;
   if (trans) {
 #pragma unroll 2
     for (int k = 0; k < TILE / 8; ++k) {
@@ -337,9 +483,9 @@ int ns_iterations(NsGroup* gs, int ng, int steps, float a, float b, float c, cud
         G3.ldo = S.ldn;
       }
     }
-    int rc = launch_gemm<BN, NS_STAGES, EPI_NS_GRAM>(p1, st, PK_GEMM_GRAM);
-    if (!rc) rc = launch_gemm<BN, NS_STAGES, EPI_NS_POLY>(p2, st, PK_GEMM_POLY);
-    if (!rc) rc = launch_gemm<BN, NS_STAGES, EPI_NS_UPDATE>(p3, st, PK_GEMM_UPDATE);
+    int rc = launch_gemm<BN, EPI_NS_GRAM>(p1, st, PK_GEMM_GRAM);
+    if (!rc) rc = launch_gemm<BN, EPI_NS_POLY>(p2, st, PK_GEMM_POLY);
+    if (!rc) rc = launch_gemm<BN, EPI_NS_UPDATE>(p3, st, PK_GEMM_UPDATE);
     if (rc) return rc;
   }
   return LSR_OK;

@@ -113,7 +113,7 @@ int check_device() {
 
 int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t inner,
                    uint64_t outer, uint64_t batch, uint64_t ld, uint64_t bstride, uint32_t box_inner,
-                   uint32_t box_outer) {
+                   uint32_t box_outer, CUtensorMapSwizzle swizzle) {
   if (!g_encode) {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -131,7 +131,7 @@ int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, 
   cuuint32_t box[3] = {box_inner, box_outer, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = g_encode(map, dtype, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? LSR_OK : LSR_ERR_DRIVER;
 }

@@ -20,7 +20,7 @@ int check_device();
 // `ld` and batch stride `bstride` (elements), 128-byte swizzle, the given box.
 int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t inner,
                    uint64_t outer, uint64_t batch, uint64_t ld, uint64_t bstride, uint32_t box_inner,
-                   uint32_t box_outer);
+                   uint32_t box_outer, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 // Launch accounting / optional per-launch timing. Kinds group the library's
 // kernels for the profile read-out (lsr_profile_read).
@@ -95,12 +95,34 @@ inline void finalize_tiles(GemmParams& p) {
   p.total_tiles = t;
 }
 
-template <int BN, int STAGES, int EPI>
+// Set up the TMA-staged epilogue of group g when its output (and aux operand)
+// satisfy the TMA alignment rules; otherwise the group keeps the direct-store
+// epilogue.
+template <int EPI>
+inline void setup_out_map(GemmParams& p, int g) {
+  using T = EpiT<EPI>;
+  GroupDesc& G = p.g[g];
+  G.tma_out = 0;
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  if (!G.out || !a16(G.out) || (G.ldo * T::ESZ) % 16 || (G.out_bs * T::ESZ) % 16 || G.N % T::EPV) return;
+  if (T::AUX && (!G.aux || !a16(G.aux) || (G.ld_aux * T::ESZ) % 16 || (G.aux_bs * T::ESZ) % 16)) return;
+  const int rows = G.out_trans ? G.N : G.M;
+  const int cols = G.out_trans ? G.M : G.N;
+  const long long bs = std::max<long long>(G.out_bs, (long long)rows * G.ldo);
+  const int rc = encode_tmap_3d(&p.mapOut[g], T::F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                                T::ESZ, G.out, (uint64_t)cols, (uint64_t)rows, (uint64_t)std::max(G.batch, 1),
+                                (uint64_t)G.ldo, (uint64_t)bs, 32u, 32u,
+                                T::F32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+  if (rc == LSR_OK) G.tma_out = 1;
+}
+
+template <int BN, int EPI, int STAGES = default_stages<EPI>()>
 inline int launch_gemm(GemmParams& p, cudaStream_t st, int kind = PK_GEMM_OTHER) {
-  using L = GemmSmem<BN, STAGES>;
+  using L = GemmSmem<BN, STAGES, EPI>;
   static_assert(L::TOTAL <= 232448, "shared memory budget exceeded");
   finalize_tiles<BN>(p);
   if (p.total_tiles == 0) return LSR_OK;
+  for (int g = 0; g < p.ngroups; ++g) setup_out_map<EPI>(p, g);
   p.status = status_ptr();
   if (!p.status) return LSR_ERR_LAUNCH;
   auto kfn = gemm_sm100_kernel<BN, STAGES, EPI>;

@@ -1,0 +1,101 @@
+"""CPU: the C-ABI library loads and exports every symbol include/lsr.h declares;
+host-side argument validation that needs no GPU; Python host logic."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "lsr.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"LSR_API\s+[\w\s\*]+?\b(lsr_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    for must in ("lsr_version", "lsr_ns_bf16", "lsr_muon_step_bf16", "lsr_muon_orthogonalize_bf16",
+                 "lsr_muon_apply_bf16", "lsr_gemm_bf16", "lsr_gram_update_f32"):
+        assert must in syms
+
+
+def test_library_exports_every_declared_symbol():
+    from lsr import _lib
+    lib = _lib.load()
+    missing = [s for s in declared_symbols() if not hasattr(lib, s)]
+    assert not missing, missing
+    # and the ctypes table covers exactly the header
+    assert set(_lib.SIGNATURES) == set(declared_symbols())
+
+
+def test_version_and_errors():
+    from lsr import _lib
+    lib = _lib.load()
+    assert b"sm_100a" in lib.lsr_version()
+    assert lib.lsr_strerror(-3) == b"workspace missing or too small"
+    assert lib.lsr_strerror(12345) == b"unknown liblsr error"
+
+
+def test_argument_validation_without_gpu():
+    from lsr import _lib
+    lib = _lib.load()
+    # bad sizes are rejected before any device work
+    assert lib.lsr_ns_bf16(None, None, -1, 4, 4, 1, 5, 1.0, 1.0, 1.0, 1e-7, None, 0, None) == -1
+    assert lib.lsr_ns_bf16(None, None, 1, 0, 4, 1, 5, 1.0, 1.0, 1.0, 1e-7, None, 0, None) == -1
+    assert lib.lsr_ns_bf16(None, None, 0, 4, 4, 1, 5, 1.0, 1.0, 1.0, 1e-7, None, 0, None) == 0  # empty batch
+    assert lib.lsr_gemm_bf16(None, None, None, 1, 0, 4, 4, 0, 0, 0, 1.0, None) == -1
+    assert lib.lsr_gram_update_f32(None, None, 1, 4, 4, 2, 0.0, 1.0, None) == -1
+    assert lib.lsr_ns_workspace_bytes(2, 64, 256, 1) > 2 * 64 * 256 * 2 * 2
+
+
+def test_workspace_sizes_scale():
+    from lsr import _lib
+    lib = _lib.load()
+    g = _lib.MuonGroup(rows=1600, cols=6400, count=48)
+    arr = (_lib.MuonGroup * 1)(g)
+    ws = lib.lsr_muon_workspace_bytes(arr, 1)
+    # two X buffers + A + B for 48 matrices, plus small scratch
+    assert ws >= 48 * (2 * 1600 * 6400 + 2 * 1600 * 1600) * 2
+    assert lib.lsr_muon_workspace_bytes(arr, -1) == 0
+
+
+def test_muon_adamw_host_logic_cpu():
+    """Parameter split, shape groups and summary follow muon_lm_ddp.py:462-542 (no GPU needed)."""
+    import lsr
+    params = [("transformer.wte.weight", torch.nn.Parameter(torch.zeros(10, 4))),
+              ("transformer.h.0.attn.c_attn.weight", torch.nn.Parameter(torch.zeros(4, 12))),
+              ("transformer.h.0.mlp.c_proj.weight", torch.nn.Parameter(torch.zeros(16, 4))),
+              ("transformer.h.0.ln_1.weight", torch.nn.Parameter(torch.zeros(4))),
+              ("lm_head.weight", torch.nn.Parameter(torch.zeros(10, 4)))]
+    params.append(("tied.wte", params[0][1]))  # tied weight: deduplicated
+    opt = lsr.MuonAdamW(params, muon_mode="batched", muon_lr=0.02, muon_momentum=0.95, muon_weight_decay=0.01,
+                        muon_nesterov=True, muon_ns_steps=5, muon_eps=1e-7, muon_lr_adjust="original",
+                        muon_batch_matrices=8, adam_lr=3e-4, adam_betas=(0.9, 0.95), adam_weight_decay=0.1, rank=0)
+    s = opt.summary()
+    assert s["muon_matrix_count"] == 2
+    assert s["muon_param_count"] == 4 * 12 + 16 * 4
+    assert s["adam_param_count"] == 10 * 4 + 4 + 10 * 4
+    assert sorted(tuple(g["oriented_shape"]) for g in s["shape_groups"]) == [(4, 12), (4, 16)]
+    opt.muon_mode = "nope"
+    with pytest.raises(ValueError):
+        opt.muon_step()
+
+
+def test_adjusted_lr_matches_oracle():
+    import lsr
+    from oracle import muon as om
+    for shape in [(1600, 4800), (6400, 1600), (3, 3)]:
+        for mode in ("original", "match_rms_adamw", "none"):
+            assert lsr.adjusted_muon_lr(0.02, shape, mode) == om.adjusted_muon_lr(0.02, shape, mode)
+
+
+def test_product_path_has_no_cpu_fallback():
+    import lsr
+    with pytest.raises(ValueError):
+        lsr.zeropower_serial(torch.zeros(8, 8, dtype=torch.bfloat16), 5, 1e-7)
+    src = "".join(p.read_text() for p in (ROOT / "cuda-lsr_b200" / "lsr").glob("*.py"))
+    assert "oracle" not in src

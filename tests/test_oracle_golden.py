@@ -1,0 +1,99 @@
+"""CPU: the numpy oracle against golden outputs of the reference's own code.
+
+The fixtures in tests/golden/ were produced by running the reference's
+functions on CPU (tests/golden/make_golden.py). These tests pin the oracle
+that the GPU parity tests then use as their checker.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import muon as om
+from oracle.bf16 import from_bits, rel_fro, round_bf16, to_bits
+
+GOLD = Path(__file__).parent / "golden"
+
+
+@pytest.fixture(scope="module")
+def mz():
+    return np.load(GOLD / "muon_golden.npz")
+
+
+def test_round_bf16_known_values():
+    x = np.array([1.0, 1.00390625, 1.005859375, -2.5, 3.4445, 0.0, -0.0, np.inf, np.nan], dtype=np.float32)
+    r = round_bf16(x)
+    assert r[0] == 1.0 and r[1] == 1.0  # tie to even
+    assert r[2] == np.float32(1.0078125)
+    assert r[3] == -2.5 and r[4] == np.float32(3.4375)
+    assert np.isinf(r[7]) and np.isnan(r[8])
+    assert np.array_equal(from_bits(to_bits(r[:8])), r[:8])
+    assert round_bf16(np.float32(1.0)).shape == ()
+
+
+def test_ns_serial_small_shapes(mz):
+    for i, (r, c) in enumerate(mz["serial_shapes"]):
+        G = from_bits(mz[f"serial{i}_in"]).reshape(r, c)
+        ref = from_bits(mz[f"serial{i}_out"]).reshape(r, c)
+        assert rel_fro(om.zeropower(G, 5, 1e-7), ref) < 2e-2, (r, c)
+
+
+def test_ns_batched(mz):
+    X = from_bits(mz["batched_in"]).reshape(3, 64, 192)
+    ref = from_bits(mz["batched_out"]).reshape(3, 64, 192)
+    assert rel_fro(om.zeropower(X, 5, 1e-7, orient=False), ref) < 2e-2
+
+
+@pytest.mark.parametrize("steps", [0, 1, 3])
+def test_ns_step_counts(mz, steps):
+    G = from_bits(mz["steps_in"]).reshape(48, 160)
+    ref = from_bits(mz[f"steps{steps}_out"]).reshape(48, 160)
+    err = rel_fro(om.zeropower(G, steps, 1e-7), ref)
+    assert err < (1e-6 if steps == 0 else 2e-2)
+
+
+def test_ns_config1_shape(mz):
+    torch = pytest.importorskip("torch")
+    g0 = torch.Generator().manual_seed(0)
+    for name, (r, c) in (("cfg1_wide", (768, 3072)), ("cfg1_tall", (3072, 768))):
+        G = (torch.randn(r, c, generator=g0) * 0.02).to(torch.bfloat16).float().numpy()
+        sums = [G.astype(np.float64).sum(), (G.astype(np.float64) ** 2).sum()]
+        assert np.allclose(sums, mz[f"{name}_in_sums"]), "torch CPU RNG changed"
+        O = om.zeropower(G, 5, 1e-7)
+        assert rel_fro(O[:64], from_bits(mz[f"{name}_out_rows"]).reshape(64, -1)) < 2e-2
+        assert rel_fro(O.astype(np.float64).sum(0), mz[f"{name}_out_colsum"]) < 2e-2
+        assert abs(np.linalg.norm(O) - mz[f"{name}_out_fro"][0]) / mz[f"{name}_out_fro"][0] < 1e-3
+
+
+def test_adjusted_lr(mz):
+    for (lr, r, c), o, m, n in zip(mz["lr_cases"], mz["lr_original"], mz["lr_match"], mz["lr_none"]):
+        assert om.adjusted_muon_lr(lr, (int(r), int(c)), "original") == pytest.approx(o)
+        assert om.adjusted_muon_lr(lr, (int(r), int(c)), "match_rms_adamw") == pytest.approx(m)
+        assert om.adjusted_muon_lr(lr, (int(r), int(c)), "none") == pytest.approx(n)
+    with pytest.raises(ValueError):
+        om.adjusted_muon_lr(0.02, (2, 3), "bogus")
+
+
+NAMES = [("h.0.attn.c_attn.weight", (64, 192)), ("h.0.attn.c_proj.weight", (64, 64)),
+         ("h.0.mlp.c_fc.weight", (64, 256)), ("h.0.mlp.c_proj.weight", (256, 64)),
+         ("h.1.mlp.c_fc.weight", (64, 256)), ("h.1.mlp.c_proj.weight", (256, 64))]
+
+
+@pytest.mark.parametrize("mode", ["batched", "serial"])
+def test_muon_two_steps(mz, mode):
+    P = [from_bits(mz[f"muon_init_{n}"]).reshape(s) for n, s in NAMES]
+    M = [np.zeros(s, np.float32) for _, s in NAMES]
+    P0 = [p.copy() for p in P]
+    for step in range(2):
+        G = [from_bits(mz[f"muon_grad{step}_{n}"]).reshape(s) for n, s in NAMES]
+        P, M = om.muon_step(P, G, M, lr=0.02, mu=0.95, nesterov=True, wd=0.01, ns_steps=5, eps=1e-7)
+    for (n, s), p, m, p0 in zip(NAMES, P, M, P0):
+        ref = from_bits(mz[f"muon_{mode}_{n}"]).reshape(s)
+        assert rel_fro(p - p0, ref - p0) < 0.1, n
+        assert np.array_equal(m, from_bits(mz[f"muon_{mode}_mom_{n}"]).reshape(s)), n
+
+
+def test_ns_flops_config4():
+    shapes = [(1600, 4800), (1600, 1600), (1600, 6400), (6400, 1600)] * 48
+    total = sum(om.ns_flops(min(s), max(s)) for s in shapes)
+    assert abs(total / 1e12 - 55.05) < 0.01
