@@ -601,6 +601,34 @@ int muon_apply(const lsr_muon_group* groups, int ngroups, const bf16* const* upd
 }
 
 }  // namespace
+
+// Newton–Schulz over a caller-provided scratch region that is already sized and
+// 256-byte aligned; used by the allocation-free entry point (noalloc.cu). It
+// makes no host or device allocation of its own.
+int ns_bf16_fixed_scratch(const void* in, void* out, int batch, int rows, int cols, int orient, int steps, float a,
+                          float b, float c, float eps, uint8_t* scratch, cudaStream_t st) {
+  const bool trans = orient && rows > cols;
+  const int m = trans ? cols : rows, n = trans ? rows : cols;
+  Carver cv{scratch};
+  NsGroup G;
+  carve_group(cv, G, batch, m, n, src_tiles(rows, cols));
+  G.final_out = out;
+  G.final_trans = trans;
+  G.final_ld = trans ? m : n;
+  G.final_bs = (long long)rows * cols;
+  MatRef src{nullptr, in, (long long)rows * cols}, none{nullptr, nullptr, 0};
+  {
+    ProfScope prof(PK_EW_ORIENT, st);
+    orient_kernel<false><<<dim3(G.nparts, batch), EW_THREADS, 0, st>>>(src, none, rows, cols, trans, G.X[0],
+                                                                      (long long)m * G.ldn, G.ldn, G.partials, 0.f, 0);
+  }
+  if (launch_ok()) return LSR_ERR_LAUNCH;
+  int rc = normalize_group(G, eps, st);
+  if (rc) return rc;
+  if (steps == 0) return copy_final(G, rows, cols, st);
+  return ns_iterations(&G, 1, steps, a, b, c, st);
+}
+
 }  // namespace lsr
 
 using namespace lsr;

@@ -23,6 +23,7 @@ _ERRORS = {
     -4: RuntimeError,
     -5: RuntimeError,
     -6: RuntimeError,
+    -7: ValueError,
 }
 
 c_int, c_float, c_size_t, c_void_p = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p
@@ -55,6 +56,11 @@ SIGNATURES: dict[str, tuple] = {
         c_int,
         [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float, c_float, c_float, c_float, c_void_p,
          c_size_t, c_void_p],
+    ),
+    "lsr_ns_noalloc_capacity": (c_size_t, []),
+    "lsr_ns_bf16_noalloc": (
+        c_int,
+        [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float, c_float, c_float, c_float, c_void_p],
     ),
     "lsr_gemm_bf16": (
         c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p]),

@@ -41,6 +41,7 @@ typedef struct CUstream_st* lsr_stream_t; /* == cudaStream_t */
 #define LSR_ERR_LAUNCH (-4)    /* kernel launch failed (cudaGetLastError)    */
 #define LSR_ERR_DRIVER (-5)    /* TMA tensor-map encoding failed             */
 #define LSR_ERR_DEVICE (-6)    /* current device is not sm_100               */
+#define LSR_ERR_TOO_LARGE (-7) /* problem exceeds the fixed scratch capacity */
 
 /* Library version string, e.g. "lsr-b200 0.1.0 (sm_100a)". */
 LSR_API const char* lsr_version(void);
@@ -87,6 +88,21 @@ LSR_API int lsr_profile_read(double* ms, long long* launches, int nkinds, int re
 LSR_API size_t lsr_ns_workspace_bytes(int batch, int rows, int cols, int orient);
 LSR_API int lsr_ns_bf16(const void* in, void* out, int batch, int rows, int cols, int orient, int steps, float a, float b,
                 float c, float eps, void* ws, size_t ws_bytes, lsr_stream_t stream);
+
+/* Allocation-free variant of lsr_ns_bf16 (same arguments minus the
+ * workspace; same kernels and results). No counterpart in the reference: it
+ * serves callers that cannot allocate device memory themselves (a host
+ * program whose device memory belongs to another allocator, or one that
+ * cannot afford the device synchronisation cudaMalloc/cudaFree may cause).
+ * Its scratch is a fixed 24 MiB device array inside the library, held by
+ * every GPU that loads the library until exit; problems whose
+ * lsr_ns_workspace_bytes() exceeds lsr_ns_noalloc_capacity() are rejected
+ * with LSR_ERR_TOO_LARGE. All calls share that array: calls that overlap on
+ * the GPU race and must be ordered by the caller. The first call on a device
+ * looks up the array's device address; make it before any stream capture. */
+LSR_API size_t lsr_ns_noalloc_capacity(void);
+LSR_API int lsr_ns_bf16_noalloc(const void* in, void* out, int batch, int rows, int cols, int orient, int steps,
+                                float a, float b, float c, float eps, lsr_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Muon step over groups of equally shaped parameter matrices.
