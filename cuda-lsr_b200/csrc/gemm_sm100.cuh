@@ -25,9 +25,10 @@
 namespace lsr {
 
 constexpr int kMaxGroups = 4;
-constexpr int kMaxSeg = 2;
+constexpr int kMaxSeg = 6;
 constexpr int BM = 128;
-constexpr int BK = 64;  // bf16 elements in one 128-byte swizzle row
+constexpr int BK = 64;       // bf16 elements in one 128-byte swizzle row (one K block)
+constexpr int BK_TF32 = 32;  // fp32 (tf32) elements in one 128-byte swizzle row
 constexpr int kGemmThreads = 192;
 constexpr int kEpiThreads = 128;
 
@@ -39,14 +40,32 @@ enum : int {
   EPI_NS_POLY = 3,     // out = bf16(bf16(alpha*aux) + bf16(beta*bf16(acc))) (symmetric)
   EPI_NS_UPDATE = 4,   // out = bf16(bf16(alpha*aux) + bf16(acc))
   EPI_F32_EMA = 5,     // out = beta * out + alpha * acc                     (fp32)
+  EPI_SPLIT_BF16X2 = 6,  // out = bf16(acc), out2 = bf16(acc - bf16(acc))   (hi/lo bf16 pair)
+  EPI_SPLIT_TF32 = 7,    // out = tf32(acc), out2 = acc - tf32(acc)        (hi/lo fp32 pair)
 };
 
+// Round an fp32 value to tf32 (10 explicit mantissa bits, nearest, ties away
+// from zero); x - tf32_hi(x) is then exact in fp32.
+__host__ __device__ __forceinline__ float tf32_hi(float x) {
+#ifdef __CUDA_ARCH__
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+#else
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  u = (u + 0x1000u) & 0xFFFFE000u;
+  float r;
+  memcpy(&r, &u, 4);
+  return r;
+#endif
+}
+
 struct SegDesc {
-  int kblocks;   // number of BK-wide K blocks
+  int kblocks;   // number of K blocks (64 bf16 / 32 tf32 elements each)
   int a_mn;      // operand A stored MN-major (rows of A are columns in memory)
   int b_mn;      // operand B stored MN-major
   int a_bcast;   // operand A is shared by the whole batch (TMA z = 0)
   int b_bcast;
+  int slot;      // dual-accumulator kernels: 0 = main products, 1 = small correction products
 };
 
 struct GroupDesc {
@@ -64,12 +83,14 @@ struct GroupDesc {
   int ld_aux;
   float alpha, beta;
   int tma_out;  // epilogue stages 32x32 chunks in smem and stores them with TMA (mapOut)
+  void* out2;   // second output of the split epilogues (same layout as out)
 };
 
 struct GemmParams {
   CUtensorMap mapA[kMaxGroups][kMaxSeg];
   CUtensorMap mapB[kMaxGroups][kMaxSeg];
-  CUtensorMap mapOut[kMaxGroups];  // output in stored orientation, box 32 x 32
+  CUtensorMap mapOut[kMaxGroups];   // output in stored orientation, box 32 x 32
+  CUtensorMap mapOut2[kMaxGroups];  // second output of the split epilogues
   GroupDesc g[kMaxGroups];
   int ngroups;
   int total_tiles;
@@ -176,7 +197,24 @@ __device__ __forceinline__ void epilogue_chunk(const GroupDesc& G, int b, int ro
   const int lo = G.tri ? max(0, row - col0) : 0;
   if (lo >= ncols) return;
 
-  if constexpr (EPI == EPI_STORE_F32 || EPI == EPI_F32_EMA) {
+  if constexpr (EPI == EPI_SPLIT_BF16X2 || EPI == EPI_SPLIT_TF32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j >= ncols) continue;
+      const long long idx = (long long)b * G.out_bs +
+                            (G.out_trans ? (long long)(col0 + j) * G.ldo + row : (long long)row * G.ldo + col0 + j);
+      if constexpr (EPI == EPI_SPLIT_TF32) {
+        const float h = tf32_hi(v[j]);
+        reinterpret_cast<float*>(G.out)[idx] = h;
+        reinterpret_cast<float*>(G.out2)[idx] = v[j] - h;
+      } else {
+        const __nv_bfloat16 h = __float2bfloat16_rn(v[j]);
+        reinterpret_cast<__nv_bfloat16*>(G.out)[idx] = h;
+        reinterpret_cast<__nv_bfloat16*>(G.out2)[idx] = __float2bfloat16_rn(v[j] - __bfloat162float(h));
+      }
+    }
+    return;
+  } else if constexpr (EPI == EPI_STORE_F32 || EPI == EPI_F32_EMA) {
     float* out = reinterpret_cast<float*>(G.out) + (long long)b * G.out_bs;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
@@ -248,7 +286,8 @@ __device__ __forceinline__ void epilogue_chunk(const GroupDesc& G, int b, int ro
 
 template <int EPI>
 struct EpiT {
-  static constexpr bool F32 = (EPI == EPI_STORE_F32 || EPI == EPI_F32_EMA);
+  static constexpr bool F32 = (EPI == EPI_STORE_F32 || EPI == EPI_F32_EMA || EPI == EPI_SPLIT_TF32);
+  static constexpr bool SPLIT = (EPI == EPI_SPLIT_BF16X2 || EPI == EPI_SPLIT_TF32);
   static constexpr int ESZ = F32 ? 4 : 2;
   static constexpr int ROWB = 32 * ESZ;  // bytes per staged row
   static constexpr int CHB = 32 * ROWB;  // bytes per staged 32x32 chunk
@@ -335,6 +374,67 @@ __device__ __forceinline__ void epilogue_chunk_staged(const GemmParams& p, int g
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = G.alpha * v[j];
   }
+  if constexpr (T::SPLIT) {
+    // hi part -> dbuf (mapOut), lo part -> tbuf (mapOut2); transposed when out_trans
+    if (G.out_trans) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const uint32_t off = stg_off<T::ROWB>(j, (lane * T::ESZ) / 16) + (lane * T::ESZ) % 16;
+        if constexpr (T::F32) {
+          const float h = tf32_hi(v[j]);
+          *reinterpret_cast<float*>(dbuf + off) = h;
+          *reinterpret_cast<float*>(tbuf + off) = v[j] - h;
+        } else {
+          const __nv_bfloat16 h = __float2bfloat16_rn(v[j]);
+          *reinterpret_cast<__nv_bfloat16*>(dbuf + off) = h;
+          *reinterpret_cast<__nv_bfloat16*>(tbuf + off) = __float2bfloat16_rn(v[j] - __bfloat162float(h));
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_3d(&p.mapOut[g], dbuf, row0, col0, b);
+        tma_store_3d(&p.mapOut2[g], tbuf, row0, col0, b);
+        bulk_commit();
+      }
+      return;
+    }
+#pragma unroll
+    for (int j = 0; j < T::VPR; ++j) {
+      uint4 uh, ul;
+      if constexpr (T::F32) {
+        float h[4], l[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          h[e] = tf32_hi(v[4 * j + e]);
+          l[e] = v[4 * j + e] - h[e];
+        }
+        uh = make_uint4(__float_as_uint(h[0]), __float_as_uint(h[1]), __float_as_uint(h[2]), __float_as_uint(h[3]));
+        ul = make_uint4(__float_as_uint(l[0]), __float_as_uint(l[1]), __float_as_uint(l[2]), __float_as_uint(l[3]));
+      } else {
+        __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(&uh);
+        __nv_bfloat162* ll = reinterpret_cast<__nv_bfloat162*>(&ul);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float a0 = v[8 * j + 2 * e], a1 = v[8 * j + 2 * e + 1];
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(a0, a1);
+          const float2 hf = __bfloat1622float2(h2);
+          hh[e] = h2;
+          ll[e] = __floats2bfloat162_rn(a0 - hf.x, a1 - hf.y);
+        }
+      }
+      *reinterpret_cast<uint4*>(dbuf + stg_off<T::ROWB>(lane, j)) = uh;
+      *reinterpret_cast<uint4*>(tbuf + stg_off<T::ROWB>(lane, j)) = ul;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(&p.mapOut[g], dbuf, col0, row0, b);
+      tma_store_3d(&p.mapOut2[g], tbuf, col0, row0, b);
+      bulk_commit();
+    }
+    return;
+  }
   const bool diag = G.tri && col0 == row0;
   const bool direct = !G.out_trans;
   const bool transposed = G.out_trans || (G.tri && col0 > row0);
@@ -392,8 +492,8 @@ __device__ __forceinline__ void epilogue_chunk_staged(const GemmParams& p, int g
 
 template <int BN, int STAGES, int EPI>
 struct GemmSmem {
-  static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int A_BYTES = BM * 128;  // 128-byte K rows, for bf16 and tf32 alike
+  static constexpr int B_BYTES = BN * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;
   static constexpr int EPI_BYTES = (kEpiThreads / 32) * 4 * EpiT<EPI>::CHB;  // per warp: 2 direct + 2 transposed
@@ -408,9 +508,21 @@ constexpr int default_stages() {
   return EpiT<EPI>::F32 ? 3 : 4;
 }
 
-template <int BN, int STAGES, int EPI>
+// TF32 = 0: bf16 operands (kind::f16); TF32 = 1: fp32 operands read as tf32
+// (kind::tf32). Both use 128-byte K rows: 64 bf16 or 32 fp32 per K block, four
+// UMMAs of K = 16 (bf16) / 8 (tf32) per block.
+// DUAL = 1: each tile owns two TMEM accumulators (segment slot 0 and 1) that
+// the epilogue adds in fp32; the tensor core's accumulation then never adds
+// small correction products into a large running sum (3xTF32 accuracy). One
+// tile's accumulators fill TMEM, so tiles are not double-buffered.
+template <int BN, int STAGES, int EPI, int TF32, int DUAL>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __grid_constant__ GemmParams p) {
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 64 in [64, 256]");
+  constexpr int KE = TF32 ? BK_TF32 : BK;        // elements per K block (= MN elements per MN-major chunk)
+  constexpr int CHUNK = KE * 128;                // bytes of one MN-major chunk (KE K-rows of 128 B)
+  constexpr uint32_t MN_STEP = (TF32 ? 8 : 16) * 128;  // bytes between UMMA K steps, MN-major
+  constexpr int ACC_COLS = DUAL ? 2 * BN : BN;          // TMEM columns per tile in flight
+  static_assert(2 * BN <= 512, "two BN-wide accumulators must fit in TMEM");
   using L = GemmSmem<BN, STAGES, EPI>;
   using ET = EpiT<EPI>;
   extern __shared__ uint8_t smem_raw[];
@@ -482,18 +594,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
             uint8_t* sa = smem + s * L::STAGE_BYTES;
             uint8_t* sb = sa + L::A_BYTES;
             mbar_arrive_expect_tx(full + s, L::STAGE_BYTES);
-            const int k0 = kb * BK;
+            const int k0 = kb * KE;
             if (!S.a_mn) {
               tma_load_3d(sa, ma, full + s, k0, m0, za);
             } else {
 #pragma unroll
-              for (int c = 0; c < BM / 64; ++c) tma_load_3d(sa + c * 8192, ma, full + s, m0 + 64 * c, k0, za);
+              for (int c = 0; c < BM / KE; ++c) tma_load_3d(sa + c * CHUNK, ma, full + s, m0 + KE * c, k0, za);
             }
             if (!S.b_mn) {
               tma_load_3d(sb, mb, full + s, k0, n0, zb);
             } else {
 #pragma unroll
-              for (int c = 0; c < BN / 64; ++c) tma_load_3d(sb + c * 8192, mb, full + s, n0 + 64 * c, k0, zb);
+              for (int c = 0; c < BN / KE; ++c) tma_load_3d(sb + c * CHUNK, mb, full + s, n0 + KE * c, k0, zb);
             }
             if (++s == STAGES) {
               s = 0;
@@ -518,14 +630,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
         const GroupDesc& G = p.g[g];
         if (!mbar_wait(tempty + acc, aph ^ 1, abort_flag, p.status, ST_TIMEOUT_MMA_TMEM)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        uint32_t accumulate = 0;
+        const uint32_t d_base = tmem_base + static_cast<uint32_t>(acc * ACC_COLS);
+        uint32_t acc_flags = 0;  // bit s: slot s already holds a partial sum
         for (int sg = 0; ok && sg < G.nseg; ++sg) {
           const SegDesc S = G.seg[sg];
-          const uint32_t idesc = make_idesc(BM, BN, 1u, (uint32_t)S.a_mn, (uint32_t)S.b_mn);
-          // per-UMMA_K (16 elements) descriptor advance, in 16-byte units
-          const uint32_t a_step = S.a_mn ? (2048u >> 4) : (32u >> 4);
-          const uint32_t b_step = S.b_mn ? (2048u >> 4) : (32u >> 4);
+          const int slot = DUAL ? S.slot : 0;
+          const uint32_t d_tmem = d_base + static_cast<uint32_t>(slot * BN);
+          uint32_t accumulate = (acc_flags >> slot) & 1u;
+          acc_flags |= 1u << slot;
+          const uint32_t idesc = make_idesc(BM, BN, TF32 ? 2u : 1u, (uint32_t)S.a_mn, (uint32_t)S.b_mn);
+          // per-UMMA descriptor advance along K, in 16-byte units: 32 B within a
+          // K-major row, MN_STEP bytes (UMMA_K rows) for MN-major
+          const uint32_t a_step = S.a_mn ? (MN_STEP >> 4) : (32u >> 4);
+          const uint32_t b_step = S.b_mn ? (MN_STEP >> 4) : (32u >> 4);
           for (int kb = 0; kb < S.kblocks; ++kb) {
             if (!mbar_wait(full + s, ph, abort_flag, p.status, ST_TIMEOUT_MMA_FULL)) {
               ok = false;
@@ -534,11 +651,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
             tc_fence_after();
             const uint32_t sa = smem_u32(smem + s * L::STAGE_BYTES);
             const uint32_t sb = sa + L::A_BYTES;
-            const uint64_t adesc = S.a_mn ? smem_desc_sw128(sa, 8192, 1024) : smem_desc_sw128(sa, 16, 1024);
-            const uint64_t bdesc = S.b_mn ? smem_desc_sw128(sb, 8192, 1024) : smem_desc_sw128(sb, 16, 1024);
+            const uint64_t adesc = S.a_mn ? smem_desc_sw128(sa, CHUNK, 1024) : smem_desc_sw128(sa, 16, 1024);
+            const uint64_t bdesc = S.b_mn ? smem_desc_sw128(sb, CHUNK, 1024) : smem_desc_sw128(sb, 16, 1024);
 #pragma unroll
-            for (int k = 0; k < BK / 16; ++k) {
-              umma_bf16(d_tmem, adesc + (uint64_t)(k * a_step), bdesc + (uint64_t)(k * b_step), idesc, accumulate);
+            for (int k = 0; k < 4; ++k) {
+              if constexpr (TF32)
+                umma_tf32(d_tmem, adesc + (uint64_t)(k * a_step), bdesc + (uint64_t)(k * b_step), idesc, accumulate);
+              else
+                umma_bf16(d_tmem, adesc + (uint64_t)(k * a_step), bdesc + (uint64_t)(k * b_step), idesc, accumulate);
               accumulate = 1;
             }
             umma_commit(empty + s);  // frees this smem stage once the MMAs have read it
@@ -550,8 +670,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
         }
         if (!ok) break;
         umma_commit(tfull + acc);  // accumulator ready for the epilogue
-        acc ^= 1;
-        if (acc == 0) aph ^= 1;
+        if (DUAL) {
+          aph ^= 1;
+        } else {
+          acc ^= 1;
+          if (acc == 0) aph ^= 1;
+        }
       }
       // Drain: make sure no MMA is still writing TMEM before it is released.
       umma_commit(done_bar);
@@ -593,7 +717,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
       }
       if (!mbar_wait(tfull + acc, aph, abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * ACC_COLS);
+      bool second = false;  // dual: does slot 1 hold products for this group?
+      if (DUAL) {
+        for (int sg = 0; sg < G.nseg; ++sg) second |= (G.seg[sg].slot == 1);
+      }
       uint32_t rem = live;
       while (rem) {
         const int cc = __ffs(rem) - 1;
@@ -601,6 +730,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
         const int col0 = tj * BN + cc * 32;
         uint32_t r[32];
         tmem_ld32(tbase + static_cast<uint32_t>(cc * 32), r);
+        if (DUAL && second) {
+          uint32_t r2[32];
+          tmem_ld32(tbase + static_cast<uint32_t>(BN + cc * 32), r2);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(r2[j]));
+        }
         if (G.tma_out) {
           uint4 cur[ET::VPR];
 #pragma unroll
@@ -620,8 +756,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
       }
       tc_fence_before();
       mbar_arrive(tempty + acc);
-      acc ^= 1;
-      if (acc == 0) aph ^= 1;
+      if (DUAL) {
+        aph ^= 1;
+      } else {
+        acc ^= 1;
+        if (acc == 0) aph ^= 1;
+      }
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();

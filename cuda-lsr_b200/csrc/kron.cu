@@ -1,0 +1,394 @@
+// Kronecker operators on the tcgen05 engine (gemm_sm100.cuh).
+//
+//   Kronecker sum    (A ⊕ B) vec(X) = vec(A X + X B^T)          one kernel, one
+//                    accumulator: the two products are two K segments of the
+//                    same tile, so A ⊗ I and I ⊗ B are never formed.
+//   Kronecker apply  Y = Σ_s A_s X B_s^T  (row-major vec: (A ⊗ B) vec(X))
+//                    two chained GEMMs per term; the intermediate is written as
+//                    a hi + lo pair by the first GEMM's epilogue so that the
+//                    second product keeps fp32-level accuracy.
+//
+// Reference: hft_fused.py:89-319 (kron_sum_64x8_kernel, S-term apply, SIMT fp32)
+// and hft.py:108-140 / hft_fused.py:463-509 (kron_apply_shared_2d, torch).
+//
+// bf16 variants: bf16 operands, fp32 accumulation, fp32 output.
+// fp32 variants: every fp32 operand x is split as hi = tf32(x), lo = x - hi and
+// each product a*b is evaluated as hi*hi + hi*lo + lo*hi on kind::tf32 tensor
+// cores (the "3xTF32" emulation of fp32 GEMM); the neglected lo*lo term and
+// the tf32 truncation of lo are below 2^-21 relative. tf32 operands are always
+// given to the tensor core K-major (MN-major tf32 operands read as zero on this
+// part): the split pass writes a transposed copy where a product needs one, and
+// the intermediate of a right-first apply is stored transposed by its epilogue.
+#include "runtime.cuh"
+
+namespace lsr {
+namespace {
+
+constexpr int K_BN = 256;
+constexpr int SPLIT_THREADS = 256;
+
+// hi = tf32(x), lo = x - hi over n elements.
+__global__ void __launch_bounds__(SPLIT_THREADS) split_tf32_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                                                   float* __restrict__ lo, long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    const float h = tf32_hi(v);
+    hi[i] = h;
+    lo[i] = v - h;
+  }
+}
+
+// Transposing split: for each of `batch` R x C matrices, hi[b][c][r] = tf32(x[b][r][c]),
+// lo = x - hi. One block per 32x32 tile (blockIdx.z = matrix).
+__global__ void __launch_bounds__(SPLIT_THREADS) split_tf32_t_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                                                     float* __restrict__ lo, int R, int C) {
+  __shared__ float tile[32][33];
+  const long long base = (long long)blockIdx.z * R * C;
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 8 rows per pass
+  for (int i = ty; i < 32; i += 8) {
+    const int r = r0 + i, c = c0 + tx;
+    tile[i][tx] = (r < R && c < C) ? x[base + (long long)r * C + c] : 0.f;
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int c = c0 + i, r = r0 + tx;  // output row c, column r
+    if (c < C && r < R) {
+      const float v = tile[tx][i];
+      const float h = tf32_hi(v);
+      hi[base + (long long)c * R + r] = h;
+      lo[base + (long long)c * R + r] = v - h;
+    }
+  }
+}
+
+int launch_ok() { return cudaGetLastError() == cudaSuccess ? LSR_OK : LSR_ERR_LAUNCH; }
+
+int split_tf32(const float* x, float* hi, float* lo, long long n, cudaStream_t st) {
+  if (n <= 0) return LSR_OK;
+  const int blocks = (int)std::min<long long>((n + SPLIT_THREADS - 1) / SPLIT_THREADS, 148LL * 16);
+  ProfScope prof(PK_EW_OTHER, st);
+  split_tf32_kernel<<<blocks, SPLIT_THREADS, 0, st>>>(x, hi, lo, n);
+  return launch_ok();
+}
+
+// Split `batch` R x C matrices into transposed hi/lo copies ([batch][C][R]).
+int split_tf32_t(const float* x, float* hi, float* lo, int batch, int R, int C, cudaStream_t st) {
+  if (batch <= 0) return LSR_OK;
+  ProfScope prof(PK_EW_OTHER, st);
+  split_tf32_t_kernel<<<dim3(cdiv(C, 32), cdiv(R, 32), batch), SPLIT_THREADS, 0, st>>>(x, hi, lo, R, C);
+  return launch_ok();
+}
+
+size_t a256(size_t x) { return align_up(x, 256); }
+
+bool kron_dims_ok(int batch, int m, int n, int nterms) {
+  return batch >= 0 && batch <= 65535 && m > 0 && n > 0 && nterms > 0 && nterms <= 65535;
+}
+
+// Operand helpers (all matrices row-major).
+//   mat(base, rows, cols, batch, mn, f32): `batch` matrices rows x cols, ld = cols.
+Operand mat(const void* base, int rows, int cols, int batch, int mn, int f32) {
+  Operand o{base, rows, cols, cols, (long long)rows * cols, batch, mn};
+  o.f32 = f32;
+  return o;
+}
+
+}  // namespace
+}  // namespace lsr
+
+using namespace lsr;
+
+extern "C" {
+
+// ---------------------------------------------------------------------------
+// Kronecker sum
+// ---------------------------------------------------------------------------
+
+size_t lsr_kron_sum_workspace_bytes(int batch, int m, int n, int f32) {
+  if (!kron_dims_ok(batch, m, n, 1)) return 0;
+  if (!f32) return 0;
+  // hi/lo copies of A, B, X and X^T
+  return 2 * (a256((size_t)m * m * 4) + a256((size_t)n * n * 4) + 2 * a256((size_t)batch * m * n * 4)) + 256;
+}
+
+int lsr_kron_sum_bf16(const void* A, const void* X, const void* B, float* Y, int batch, int m, int n,
+                      lsr_stream_t stream) {
+  if (!kron_dims_ok(batch, m, n, 1)) return LSR_ERR_ARG;
+  if (batch == 0) return LSR_OK;
+  if (!A || !X || !B || !Y) return LSR_ERR_ARG;
+  int rc = check_device();
+  if (rc) return rc;
+  GemmParams p{};
+  p.ngroups = 1;
+  GroupDesc& G = p.g[0];
+  G.batch = batch;
+  G.M = m;
+  G.N = n;
+  G.nseg = 2;
+  // segment 0: A (K-major, shared) x X (MN-major): sum_k A[r][k] X[k][c]
+  rc = make_operand_map(&p.mapA[0][0], mat(A, m, m, 1, 0, 0), false, K_BN);
+  if (!rc) rc = make_operand_map(&p.mapB[0][0], mat(X, m, n, batch, 1, 0), true, K_BN);
+  // segment 1: X (K-major) x B (K-major, shared): sum_k X[r][k] B[c][k]
+  if (!rc) rc = make_operand_map(&p.mapA[0][1], mat(X, m, n, batch, 0, 0), false, K_BN);
+  if (!rc) rc = make_operand_map(&p.mapB[0][1], mat(B, n, n, 1, 0, 0), true, K_BN);
+  if (rc) return rc;
+  G.seg[0] = SegDesc{cdiv(m, BK), 0, 1, 1, 0};
+  G.seg[1] = SegDesc{cdiv(n, BK), 0, 0, 0, 1};
+  G.out = Y;
+  G.out_bs = (long long)m * n;
+  G.ldo = n;
+  G.alpha = 1.f;
+  return launch_gemm<K_BN, EPI_STORE_F32>(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int lsr_kron_sum_f32(const float* A, const float* X, const float* B, float* Y, int batch, int m, int n, void* ws,
+                     size_t ws_bytes, lsr_stream_t stream) {
+  if (!kron_dims_ok(batch, m, n, 1)) return LSR_ERR_ARG;
+  if (batch == 0) return LSR_OK;
+  if (!A || !X || !B || !Y) return LSR_ERR_ARG;
+  int rc = check_device();
+  if (rc) return rc;
+  if (!ws || ws_bytes < lsr_kron_sum_workspace_bytes(batch, m, n, 1)) return LSR_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* w = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(ws), 256));
+  float* Ah = reinterpret_cast<float*>(w);
+  float* Al = reinterpret_cast<float*>(w += a256((size_t)m * m * 4));
+  float* Bh = reinterpret_cast<float*>(w += a256((size_t)m * m * 4));
+  float* Bl = reinterpret_cast<float*>(w += a256((size_t)n * n * 4));
+  float* Xh = reinterpret_cast<float*>(w += a256((size_t)n * n * 4));
+  float* Xl = reinterpret_cast<float*>(w += a256((size_t)batch * m * n * 4));
+  float* Xth = reinterpret_cast<float*>(w += a256((size_t)batch * m * n * 4));
+  float* Xtl = reinterpret_cast<float*>(w += a256((size_t)batch * m * n * 4));
+  rc = split_tf32(A, Ah, Al, (long long)m * m, st);
+  if (!rc) rc = split_tf32(B, Bh, Bl, (long long)n * n, st);
+  if (!rc) rc = split_tf32(X, Xh, Xl, (long long)batch * m * n, st);
+  if (!rc) rc = split_tf32_t(X, Xth, Xtl, batch, m, n, st);
+  if (rc) return rc;
+  GemmParams p{};
+  p.ngroups = 1;
+  GroupDesc& G = p.g[0];
+  G.batch = batch;
+  G.M = m;
+  G.N = n;
+  G.nseg = 6;
+  const float* left[3][2] = {{Ah, Xth}, {Ah, Xtl}, {Al, Xth}};  // A X   : hi*hi + hi*lo + lo*hi
+  const float* right[3][2] = {{Xh, Bh}, {Xh, Bl}, {Xl, Bh}};     // X B^T : hi*hi + hi*lo + lo*hi
+  for (int t = 0; t < 3 && !rc; ++t) {
+    // A X: B operand element (c, k) = X[k][c] = X^T[c][k], K-major in the transposed copy
+    rc = make_operand_map(&p.mapA[0][t], mat(left[t][0], m, m, 1, 0, 1), false, K_BN);
+    if (!rc) rc = make_operand_map(&p.mapB[0][t], mat(left[t][1], n, m, batch, 0, 1), true, K_BN);
+    if (!rc) rc = make_operand_map(&p.mapA[0][3 + t], mat(right[t][0], m, n, batch, 0, 1), false, K_BN);
+    if (!rc) rc = make_operand_map(&p.mapB[0][3 + t], mat(right[t][1], n, n, 1, 0, 1), true, K_BN);
+    G.seg[t] = SegDesc{cdiv(m, BK_TF32), 0, 0, 1, 0, t > 0};
+    G.seg[3 + t] = SegDesc{cdiv(n, BK_TF32), 0, 0, 0, 1, t > 0};
+  }
+  if (rc) return rc;
+  G.out = Y;
+  G.out_bs = (long long)m * n;
+  G.ldo = n;
+  G.alpha = 1.f;
+  return launch_gemm<K_BN, EPI_STORE_F32, default_stages<EPI_STORE_F32>(), 1, 1>(p, st);
+}
+
+// ---------------------------------------------------------------------------
+// Kronecker apply  Y[i] = sum_s A_s X[i] B_s^T
+// ---------------------------------------------------------------------------
+
+size_t lsr_kron_apply_workspace_bytes(int batch, int m, int n, int nterms, int f32) {
+  if (!kron_dims_ok(batch, m, n, nterms)) return 0;
+  const size_t mn = (size_t)batch * m * n;
+  if (!f32) return 2 * a256(mn * 2) + 256;  // bf16 hi/lo intermediate
+  // fp32: hi/lo of A (K-major), B, X (one orientation) and of the fp32 intermediate
+  return 2 * (a256((size_t)nterms * m * m * 4) + a256((size_t)nterms * n * n * 4) + a256(mn * 4) + a256(mn * 4)) +
+         256;
+}
+
+namespace {
+
+// Fill one GEMM group from a list of (A operand, B operand) pairs.
+int set_segments(GemmParams& p, const Operand (*pairs)[2], const SegDesc* segs, int nseg) {
+  int rc = 0;
+  for (int t = 0; t < nseg && !rc; ++t) {
+    rc = make_operand_map(&p.mapA[0][t], pairs[t][0], false, K_BN);
+    if (!rc) rc = make_operand_map(&p.mapB[0][t], pairs[t][1], true, K_BN);
+    p.g[0].seg[t] = segs[t];
+  }
+  p.g[0].nseg = nseg;
+  return rc;
+}
+
+void set_out(GroupDesc& G, int batch, int m, int n, void* out, void* out2, int out_trans) {
+  G.batch = batch;
+  G.M = m;
+  G.N = n;
+  G.out = out;
+  G.out2 = out2;
+  G.out_bs = (long long)m * n;
+  G.ldo = out_trans ? m : n;
+  G.out_trans = out_trans;
+  G.alpha = 1.f;
+}
+
+// One term, bf16 operands: Y (+)= A X B^T with the cheaper association first;
+// the intermediate is a bf16 hi + lo pair (two K segments in the second GEMM).
+//   right-first (n > m): U = X B^T -> Y = A U   (U read MN-major)
+//   left-first          : T = A X  -> Y = T B^T (X read MN-major)
+int kron_term_bf16(const void* A, int a_trans, const void* X, const void* B, float* Y, void* Th, void* Tl, int batch,
+                   int m, int n, int accumulate, cudaStream_t st) {
+  const bool right_first = n > m;
+  const Operand Aop = mat(A, m, m, 1, a_trans ? 1 : 0, 0);  // A[r][k], or A^T stored [k][r]
+  const int am = a_trans ? 1 : 0;
+  {
+    GemmParams p{};
+    p.ngroups = 1;
+    set_out(p.g[0], batch, m, n, Th, Tl, 0);
+    int rc;
+    if (right_first) {
+      const Operand pr[1][2] = {{mat(X, m, n, batch, 0, 0), mat(B, n, n, 1, 0, 0)}};
+      const SegDesc sg[1] = {SegDesc{cdiv(n, BK), 0, 0, 0, 1}};
+      rc = set_segments(p, pr, sg, 1);
+    } else {
+      const Operand pr[1][2] = {{Aop, mat(X, m, n, batch, 1, 0)}};
+      const SegDesc sg[1] = {SegDesc{cdiv(m, BK), am, 1, 1, 0}};
+      rc = set_segments(p, pr, sg, 1);
+    }
+    if (!rc) rc = launch_gemm<K_BN, EPI_SPLIT_BF16X2>(p, st);
+    if (rc) return rc;
+  }
+  GemmParams p{};
+  p.ngroups = 1;
+  GroupDesc& G = p.g[0];
+  set_out(G, batch, m, n, Y, nullptr, 0);
+  G.aux = Y;
+  G.aux_bs = (long long)m * n;
+  G.ld_aux = n;
+  G.beta = accumulate ? 1.f : 0.f;
+  int rc;
+  if (right_first) {
+    const Operand pr[2][2] = {{Aop, mat(Th, m, n, batch, 1, 0)}, {Aop, mat(Tl, m, n, batch, 1, 0)}};
+    const SegDesc sg[2] = {SegDesc{cdiv(m, BK), am, 1, 1, 0}, SegDesc{cdiv(m, BK), am, 1, 1, 0}};
+    rc = set_segments(p, pr, sg, 2);
+  } else {
+    const Operand pr[2][2] = {{mat(Th, m, n, batch, 0, 0), mat(B, n, n, 1, 0, 0)},
+                              {mat(Tl, m, n, batch, 0, 0), mat(B, n, n, 1, 0, 0)}};
+    const SegDesc sg[2] = {SegDesc{cdiv(n, BK), 0, 0, 0, 1}, SegDesc{cdiv(n, BK), 0, 0, 0, 1}};
+    rc = set_segments(p, pr, sg, 2);
+  }
+  return rc ? rc : launch_gemm<K_BN, EPI_F32_EMA>(p, st);
+}
+
+// One term, fp32 operands as tf32 hi/lo pairs (3xTF32), every operand K-major:
+//   right-first: U = X B^T, stored transposed (U^T, [n][m]) as a tf32 pair -> Y = A U
+//   left-first : T = A X with X^T given -> T stored as a tf32 pair -> Y = T B^T
+// Ah/Al: K-major A; Bh/Bl: B; Xh/Xl: X (right-first) or X^T (left-first).
+int kron_term_f32(const float* Ah, const float* Al, const float* Xh, const float* Xl, const float* Bh, const float* Bl,
+                  float* Y, float* Th, float* Tl, int batch, int m, int n, int accumulate, cudaStream_t st) {
+  const bool right_first = n > m;
+  {
+    GemmParams p{};
+    p.ngroups = 1;
+    int rc;
+    if (right_first) {
+      set_out(p.g[0], batch, m, n, Th, Tl, 1);
+      const Operand pr[3][2] = {{mat(Xh, m, n, batch, 0, 1), mat(Bh, n, n, 1, 0, 1)},
+                                {mat(Xh, m, n, batch, 0, 1), mat(Bl, n, n, 1, 0, 1)},
+                                {mat(Xl, m, n, batch, 0, 1), mat(Bh, n, n, 1, 0, 1)}};
+      const SegDesc sd{cdiv(n, BK_TF32), 0, 0, 0, 1, 0}, sc{cdiv(n, BK_TF32), 0, 0, 0, 1, 1};
+      const SegDesc sg[3] = {sd, sc, sc};
+      rc = set_segments(p, pr, sg, 3);
+    } else {
+      set_out(p.g[0], batch, m, n, Th, Tl, 0);
+      const Operand pr[3][2] = {{mat(Ah, m, m, 1, 0, 1), mat(Xh, n, m, batch, 0, 1)},
+                                {mat(Ah, m, m, 1, 0, 1), mat(Xl, n, m, batch, 0, 1)},
+                                {mat(Al, m, m, 1, 0, 1), mat(Xh, n, m, batch, 0, 1)}};
+      const SegDesc sd{cdiv(m, BK_TF32), 0, 0, 1, 0, 0}, sc{cdiv(m, BK_TF32), 0, 0, 1, 0, 1};
+      const SegDesc sg[3] = {sd, sc, sc};
+      rc = set_segments(p, pr, sg, 3);
+    }
+    if (!rc) rc = launch_gemm<K_BN, EPI_SPLIT_TF32, default_stages<EPI_SPLIT_TF32>(), 1, 1>(p, st);
+    if (rc) return rc;
+  }
+  GemmParams p{};
+  p.ngroups = 1;
+  GroupDesc& G = p.g[0];
+  set_out(G, batch, m, n, Y, nullptr, 0);
+  G.aux = Y;
+  G.aux_bs = (long long)m * n;
+  G.ld_aux = n;
+  G.beta = accumulate ? 1.f : 0.f;
+  int rc;
+  if (right_first) {
+    // Y = A U: B operand element (c, k) = U[k][c] = U^T[c][k] (rows n, cols m)
+    const Operand pr[3][2] = {{mat(Ah, m, m, 1, 0, 1), mat(Th, n, m, batch, 0, 1)},
+                              {mat(Ah, m, m, 1, 0, 1), mat(Tl, n, m, batch, 0, 1)},
+                              {mat(Al, m, m, 1, 0, 1), mat(Th, n, m, batch, 0, 1)}};
+    const SegDesc sd{cdiv(m, BK_TF32), 0, 0, 1, 0, 0}, sc{cdiv(m, BK_TF32), 0, 0, 1, 0, 1};
+    const SegDesc sg[3] = {sd, sc, sc};
+    rc = set_segments(p, pr, sg, 3);
+  } else {
+    const Operand pr[3][2] = {{mat(Th, m, n, batch, 0, 1), mat(Bh, n, n, 1, 0, 1)},
+                              {mat(Th, m, n, batch, 0, 1), mat(Bl, n, n, 1, 0, 1)},
+                              {mat(Tl, m, n, batch, 0, 1), mat(Bh, n, n, 1, 0, 1)}};
+    const SegDesc sd{cdiv(n, BK_TF32), 0, 0, 0, 1, 0}, sc{cdiv(n, BK_TF32), 0, 0, 0, 1, 1};
+    const SegDesc sg[3] = {sd, sc, sc};
+    rc = set_segments(p, pr, sg, 3);
+  }
+  return rc ? rc : launch_gemm<K_BN, EPI_F32_EMA, default_stages<EPI_F32_EMA>(), 1, 1>(p, st);
+}
+
+int kron_apply(const void* A, int a_trans, const void* X, const void* B, float* Y, int batch, int m, int n,
+               int nterms, int f32, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (!kron_dims_ok(batch, m, n, nterms)) return LSR_ERR_ARG;
+  if (batch == 0) return LSR_OK;
+  if (!A || !X || !B || !Y) return LSR_ERR_ARG;
+  int rc = check_device();
+  if (rc) return rc;
+  if (!ws || ws_bytes < lsr_kron_apply_workspace_bytes(batch, m, n, nterms, f32)) return LSR_ERR_WORKSPACE;
+  uint8_t* w = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(ws), 256));
+  const size_t mn = (size_t)batch * m * n;
+  if (!f32) {
+    void* Th = w;
+    void* Tl = w + a256(mn * 2);
+    for (int s = 0; s < nterms && !rc; ++s) {
+      const void* As = static_cast<const uint8_t*>(A) + (size_t)s * m * m * 2;
+      const void* Bs = static_cast<const uint8_t*>(B) + (size_t)s * n * n * 2;
+      rc = kron_term_bf16(As, a_trans, X, Bs, Y, Th, Tl, batch, m, n, s > 0, st);
+    }
+    return rc;
+  }
+  float* Ah = reinterpret_cast<float*>(w);
+  float* Al = reinterpret_cast<float*>(w += a256((size_t)nterms * m * m * 4));
+  float* Bh = reinterpret_cast<float*>(w += a256((size_t)nterms * m * m * 4));
+  float* Bl = reinterpret_cast<float*>(w += a256((size_t)nterms * n * n * 4));
+  float* Xh = reinterpret_cast<float*>(w += a256((size_t)nterms * n * n * 4));
+  float* Xl = reinterpret_cast<float*>(w += a256(mn * 4));
+  float* Th = reinterpret_cast<float*>(w += a256(mn * 4));
+  float* Tl = reinterpret_cast<float*>(w += a256(mn * 4));
+  const float* Af = static_cast<const float*>(A);
+  // A as K-major tf32 pairs (the caller may hold A^T); B as pairs; X in the orientation the association needs
+  rc = a_trans ? split_tf32_t(Af, Ah, Al, nterms, m, m, st) : split_tf32(Af, Ah, Al, (long long)nterms * m * m, st);
+  if (!rc) rc = split_tf32(static_cast<const float*>(B), Bh, Bl, (long long)nterms * n * n, st);
+  if (!rc)
+    rc = (n > m) ? split_tf32(static_cast<const float*>(X), Xh, Xl, (long long)mn, st)
+                 : split_tf32_t(static_cast<const float*>(X), Xh, Xl, batch, m, n, st);
+  for (int s = 0; s < nterms && !rc; ++s) {
+    const size_t ao = (size_t)s * m * m, bo = (size_t)s * n * n;
+    rc = kron_term_f32(Ah + ao, Al + ao, Xh, Xl, Bh + bo, Bl + bo, Y, Th, Tl, batch, m, n, s > 0, st);
+  }
+  return rc;
+}
+
+}  // namespace
+
+int lsr_kron_apply_bf16(const void* A, int a_trans, const void* X, const void* B, float* Y, int batch, int m, int n,
+                        int nterms, void* ws, size_t ws_bytes, lsr_stream_t stream) {
+  return kron_apply(A, a_trans, X, B, Y, batch, m, n, nterms, 0, ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int lsr_kron_apply_f32(const float* A, int a_trans, const float* X, const float* B, float* Y, int batch, int m, int n,
+                       int nterms, void* ws, size_t ws_bytes, lsr_stream_t stream) {
+  return kron_apply(A, a_trans, X, B, Y, batch, m, n, nterms, 1, ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

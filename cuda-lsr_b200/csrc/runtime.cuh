@@ -2,6 +2,7 @@
 #pragma once
 
 #include <algorithm>
+#include <cstring>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -64,14 +65,17 @@ struct Operand {
   long long bs;
   int batch;
   int mn;
+  int f32 = 0;  // fp32 storage read as tf32 (else bf16)
 };
 
-// Tensor map for operand A (is_b = false, box rows BM) or B (box rows BN).
+// Tensor map for operand A (is_b = false, box rows BM) or B (box rows BN):
+// K-major box = one 128-byte K row x rows; MN-major box = 128 bytes of MN x one K block.
 inline int make_operand_map(CUtensorMap* map, const Operand& o, bool is_b, int BN) {
-  const uint32_t box_outer = o.mn ? 64u : static_cast<uint32_t>(is_b ? BN : BM);
-  return encode_tmap_3d(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, o.base, (uint64_t)o.cols, (uint64_t)o.rows,
-                        (uint64_t)std::max(o.batch, 1), (uint64_t)o.ld,
-                        (uint64_t)std::max<long long>(o.bs, (long long)o.rows * o.ld), 64u, box_outer);
+  const uint32_t ke = o.f32 ? BK_TF32 : BK;
+  const uint32_t box_outer = o.mn ? ke : static_cast<uint32_t>(is_b ? BN : BM);
+  return encode_tmap_3d(map, o.f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                        o.f32 ? 4 : 2, o.base, (uint64_t)o.cols, (uint64_t)o.rows, (uint64_t)std::max(o.batch, 1),
+                        (uint64_t)o.ld, (uint64_t)std::max<long long>(o.bs, (long long)o.rows * o.ld), ke, box_outer);
 }
 
 // Fill tile counts and the flat tile numbering of every group.
@@ -113,10 +117,19 @@ inline void setup_out_map(GemmParams& p, int g) {
                                 T::ESZ, G.out, (uint64_t)cols, (uint64_t)rows, (uint64_t)std::max(G.batch, 1),
                                 (uint64_t)G.ldo, (uint64_t)bs, 32u, 32u,
                                 T::F32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
-  if (rc == LSR_OK) G.tma_out = 1;
+  if (rc != LSR_OK) return;
+  if constexpr (T::SPLIT) {
+    if (!G.out2 || !a16(G.out2)) return;
+    const int rc2 = encode_tmap_3d(&p.mapOut2[g], T::F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                                   T::ESZ, G.out2, (uint64_t)cols, (uint64_t)rows, (uint64_t)std::max(G.batch, 1),
+                                   (uint64_t)G.ldo, (uint64_t)bs, 32u, 32u,
+                                   T::F32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc2 != LSR_OK) return;
+  }
+  G.tma_out = 1;
 }
 
-template <int BN, int EPI, int STAGES = default_stages<EPI>()>
+template <int BN, int EPI, int STAGES = default_stages<EPI>(), int TF32 = 0, int DUAL = 0>
 inline int launch_gemm(GemmParams& p, cudaStream_t st, int kind = PK_GEMM_OTHER) {
   using L = GemmSmem<BN, STAGES, EPI>;
   static_assert(L::TOTAL <= 232448, "shared memory budget exceeded");
@@ -125,7 +138,7 @@ inline int launch_gemm(GemmParams& p, cudaStream_t st, int kind = PK_GEMM_OTHER)
   for (int g = 0; g < p.ngroups; ++g) setup_out_map<EPI>(p, g);
   p.status = status_ptr();
   if (!p.status) return LSR_ERR_LAUNCH;
-  auto kfn = gemm_sm100_kernel<BN, STAGES, EPI>;
+  auto kfn = gemm_sm100_kernel<BN, STAGES, EPI, TF32, DUAL>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL) != cudaSuccess)
     return LSR_ERR_LAUNCH;
   const int grid = std::min(device_sm_count(), p.total_tiles);

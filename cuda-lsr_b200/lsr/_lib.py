@@ -66,6 +66,17 @@ SIGNATURES: dict[str, tuple] = {
         c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p]),
     "lsr_gram_update_f32": (
         c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float, c_float, c_void_p]),
+    "lsr_kron_sum_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "lsr_kron_sum_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "lsr_kron_sum_f32": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "lsr_kron_apply_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "lsr_kron_apply_bf16": (
+        c_int,
+        [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "lsr_kron_apply_f32": (
+        c_int,
+        [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "lsr_muon_workspace_bytes": (c_size_t, [ctypes.POINTER(MuonGroup), c_int]),
     "lsr_muon_step_bf16": (
         c_int,

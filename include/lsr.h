@@ -177,6 +177,44 @@ LSR_API int lsr_gemm_bf16(const void* A, const void* B, void* D, int batch, int 
 LSR_API int lsr_gram_update_f32(const void* G, void* S, int batch, int rows, int cols, int side, float beta,
                                 float alpha, lsr_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Kronecker sum  (A ⊕ B) vec(X) = vec(A X + X B^T), row-major vec, batched
+ * over X [batch][m][n]; A (m x m) and B (n x n) shared by the batch; Y is
+ * fp32 [batch][m][n]. One fused kernel: both products accumulate in the same
+ * tensor-memory tile; A ⊗ I and I ⊗ B are never formed.
+ *
+ * Replaces the S = 2 case {(A, I), (I, B)} of kron_sum_64x8_kernel /
+ * kron_sum_out (hft_fused.py:89-319) and of kron_apply_shared_2d
+ * (hft.py:108-140), generalised to any m, n with m % 8 == 0 and n % 8 == 0.
+ *   _bf16: bf16 operands, fp32 accumulation.
+ *   _f32 : fp32 operands via a 3xTF32 split on tensor cores (workspace from
+ *          lsr_kron_sum_workspace_bytes(batch, m, n, 1)); m, n % 4 == 0.
+ * ---------------------------------------------------------------------- */
+LSR_API size_t lsr_kron_sum_workspace_bytes(int batch, int m, int n, int f32);
+LSR_API int lsr_kron_sum_bf16(const void* A, const void* X, const void* B, float* Y, int batch, int m, int n,
+                              lsr_stream_t stream);
+LSR_API int lsr_kron_sum_f32(const float* A, const float* X, const float* B, float* Y, int batch, int m, int n,
+                             void* ws, size_t ws_bytes, lsr_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Kronecker apply  Y[i] = sum_s A_s X[i] B_s^T  (= (sum_s A_s ⊗ B_s) vec(X)).
+ *
+ * Replaces kron_sum_out(x, at, b, out) / kron_sum_64x8_kernel<S>
+ * (hft_fused.py:89-319, there fixed to m = 64, n = 8, S in {1,2,4,8}) and
+ * kron_apply_shared_2d (hft.py:108-140, hft_fused.py:463-509); with S = 1 it
+ * is the Shampoo preconditioner apply L^{-1/4} G R^{-1/4}.
+ * A: [nterms][m][m] (a_trans = 1: the array holds A_s^T, as kron_sum_out's
+ * `at`), B: [nterms][n][n], X: [batch][m][n], Y: fp32 [batch][m][n].
+ * Each term is two chained GEMMs (the cheaper association first); the
+ * intermediate is kept as a hi + lo pair so the second product stays at fp32
+ * accuracy.  _bf16: bf16 operands.  _f32: fp32 operands (3xTF32).
+ * ---------------------------------------------------------------------- */
+LSR_API size_t lsr_kron_apply_workspace_bytes(int batch, int m, int n, int nterms, int f32);
+LSR_API int lsr_kron_apply_bf16(const void* A, int a_trans, const void* X, const void* B, float* Y, int batch,
+                                int m, int n, int nterms, void* ws, size_t ws_bytes, lsr_stream_t stream);
+LSR_API int lsr_kron_apply_f32(const float* A, int a_trans, const float* X, const float* B, float* Y, int batch,
+                               int m, int n, int nterms, void* ws, size_t ws_bytes, lsr_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

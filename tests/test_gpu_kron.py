@@ -1,0 +1,102 @@
+"""GPU parity of the Kronecker sum / apply kernels through the Python surface and C ABI.
+
+Tolerances (relative Frobenius): bf16 operands within 1e-3 of an fp32/fp64
+product of the SAME bf16-rounded operands (fp32 accumulation, fp32 output);
+fp32 operands (3xTF32) within 1e-5 of the float64 oracle.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import kron as ok
+from oracle.bf16 import rel_fro
+
+pytestmark = pytest.mark.gpu
+TOL_BF16, TOL_F32 = 1e-3, 1e-5
+GOLD = Path(__file__).parent / "golden" / "kron_golden.npz"
+
+
+def _sym(n, g, dev="cuda"):
+    M = torch.randn(n, n, generator=g, device=dev) / (n ** 0.5)
+    return ((M + M.T) / 2).contiguous()
+
+
+@pytest.mark.parametrize("shape", [(4, 1024, 1024), (3, 200, 136), (2, 64, 8), (1, 256, 512)])
+def test_kron_sum_bf16_and_f32(shape):
+    import lsr.kron as K
+    batch, m, n = shape
+    g = torch.Generator(device="cuda").manual_seed(m + n)
+    A, B = _sym(m, g), _sym(n, g)
+    X = torch.randn(batch, m, n, generator=g, device="cuda")
+    # fp32 (3xTF32)
+    Y = K.kron_sum(A, X, B)
+    ref = ok.kron_sum(X.cpu().numpy(), A.cpu().numpy(), B.cpu().numpy())
+    assert rel_fro(Y.cpu().numpy(), ref) < TOL_F32
+    # bf16 operands, compared with the exact product of the same rounded operands
+    Ab, Xb, Bb = A.bfloat16(), X.bfloat16(), B.bfloat16()
+    Yb = K.kron_sum(Ab, Xb, Bb)
+    refb = ok.kron_sum(Xb.float().cpu().numpy(), Ab.float().cpu().numpy(), Bb.float().cpu().numpy())
+    assert rel_fro(Yb.cpu().numpy(), refb) < TOL_BF16
+
+
+def test_kron_sum_matches_dense_operator():
+    """(A ⊕ B) vec(X) against the explicitly formed A⊗I + I⊗B on a small case."""
+    import lsr.kron as K
+    g = torch.Generator(device="cuda").manual_seed(5)
+    m, n = 16, 24
+    A, B = _sym(m, g), _sym(n, g)
+    X = torch.randn(3, m, n, generator=g, device="cuda")
+    W = ok.dense_operator(np.stack([A.cpu().numpy(), np.eye(m)]), np.stack([np.eye(n), B.cpu().numpy()]))
+    ref = (X.cpu().numpy().reshape(3, -1).astype(np.float64) @ W.T).reshape(3, m, n)
+    assert rel_fro(K.kron_sum(A, X, B).cpu().numpy(), ref) < TOL_F32
+
+
+@pytest.mark.parametrize("shape,S", [((3, 128, 320), 1), ((2, 320, 128), 2), ((5, 64, 8), 4), ((2, 96, 96), 3)])
+def test_kron_apply(shape, S):
+    import lsr.kron as K
+    batch, m, n = shape
+    g = torch.Generator(device="cuda").manual_seed(S * 100 + m)
+    A = torch.randn(S, m, m, generator=g, device="cuda") / m ** 0.5
+    B = torch.randn(S, n, n, generator=g, device="cuda") / n ** 0.5
+    X = torch.randn(batch, m, n, generator=g, device="cuda")
+    ref = ok.kron_apply(X.cpu().numpy(), A.cpu().numpy(), B.cpu().numpy())
+    assert rel_fro(K.kron_apply(X, A, B).cpu().numpy(), ref) < TOL_F32
+    Ab, Xb, Bb = A.bfloat16(), X.bfloat16(), B.bfloat16()
+    refb = ok.kron_apply(Xb.float().cpu().numpy(), Ab.float().cpu().numpy(), Bb.float().cpu().numpy())
+    assert rel_fro(K.kron_apply(Xb, Ab, Bb).cpu().numpy(), refb) < TOL_BF16
+
+
+def test_golden_reference_outputs():
+    """Outputs of the reference's kron_apply_shared_2d / S-term sums (tests/golden/kron_golden.npz)."""
+    import lsr.kron as K
+    z = np.load(GOLD)
+    cu = lambda k: torch.from_numpy(z[k]).cuda()  # noqa: E731
+    for i in range(3):
+        Y = K.kron_apply_shared_2d(cu(f"apply{i}_X"), cu(f"apply{i}_A"), cu(f"apply{i}_B"))
+        assert rel_fro(Y.cpu().numpy(), z[f"apply{i}_Y"]) < TOL_F32
+    for i in range(2):
+        Y = K.kron_sum(cu(f"ksum{i}_A"), cu(f"ksum{i}_X"), cu(f"ksum{i}_B"))
+        assert rel_fro(Y.cpu().numpy(), z[f"ksum{i}_Y"]) < TOL_F32
+    for S in (1, 2, 4):
+        x, A, b = cu(f"multi{S}_X"), cu(f"multi{S}_A"), cu(f"multi{S}_B")
+        out = torch.empty_like(x)
+        K.kron_sum_out(x, A.transpose(1, 2).contiguous(), b, out)
+        assert rel_fro(out.cpu().numpy(), z[f"multi{S}_Y"]) < TOL_F32
+        assert rel_fro(out.cpu().numpy(), z[f"multi{S}_Ydense"]) < TOL_F32
+
+
+def test_kron_sum_out_errors():
+    import lsr.kron as K
+    x = torch.zeros(4, 64, 8, device="cuda")
+    at = torch.zeros(2, 64, 64, device="cuda")
+    b = torch.zeros(2, 8, 8, device="cuda")
+    with pytest.raises(RuntimeError, match="must be float32"):
+        K.kron_sum_out(x.double(), at, b, torch.zeros_like(x))
+    with pytest.raises(RuntimeError, match="b must have shape"):
+        K.kron_sum_out(x, at, torch.zeros(3, 8, 8, device="cuda"), torch.zeros_like(x))
+    with pytest.raises(RuntimeError, match="out must match"):
+        K.kron_sum_out(x, at, b, torch.zeros(4, 64, 4, device="cuda"))
+    with pytest.raises(RuntimeError, match="must be CUDA"):
+        K.kron_sum_out(x.cpu(), at, b, torch.zeros_like(x))

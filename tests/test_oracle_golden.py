@@ -97,3 +97,22 @@ def test_ns_flops_config4():
     shapes = [(1600, 4800), (1600, 1600), (1600, 6400), (6400, 1600)] * 48
     total = sum(om.ns_flops(min(s), max(s)) for s in shapes)
     assert abs(total / 1e12 - 55.05) < 0.01
+
+
+# ---------------------------------------------------------------- Kronecker oracle
+def test_kron_oracle_matches_reference_golden():
+    from oracle import kron as ok
+    z = np.load(GOLD / "kron_golden.npz")
+    for i in range(3):
+        Y = ok.kron_apply_shared_2d(z[f"apply{i}_X"], z[f"apply{i}_A"], z[f"apply{i}_B"])
+        assert rel_fro(Y, z[f"apply{i}_Y"]) < 1e-6
+    for i in range(2):
+        Y = ok.kron_sum(z[f"ksum{i}_X"], z[f"ksum{i}_A"], z[f"ksum{i}_B"])
+        assert rel_fro(Y, z[f"ksum{i}_Y"]) < 1e-6
+    for S in (1, 2, 4):
+        X, A, B = z[f"multi{S}_X"], z[f"multi{S}_A"], z[f"multi{S}_B"]
+        Y = ok.kron_apply(X, A, B)
+        assert rel_fro(Y, z[f"multi{S}_Y"]) < 1e-6
+        W = ok.dense_operator(A, B)
+        Yd = (X.reshape(X.shape[0], -1).astype(np.float64) @ W.T).reshape(X.shape)
+        assert rel_fro(Yd, z[f"multi{S}_Ydense"]) < 1e-6
