@@ -42,6 +42,9 @@ enum : int {
   EPI_F32_EMA = 5,     // out = beta * out + alpha * acc                     (fp32)
   EPI_SPLIT_BF16X2 = 6,  // out = bf16(acc), out2 = bf16(acc - bf16(acc))   (hi/lo bf16 pair)
   EPI_SPLIT_TF32 = 7,    // out = tf32(acc), out2 = acc - tf32(acc)        (hi/lo fp32 pair)
+  EPI_SOAP_ADAM = 8,     // Adam in the rotated basis on g = acc, fp32 moments st_m / st_v:
+                         //   m = b1 m + (1-b1) g ; v = b2 v + (1-b2) g^2
+                         //   u = (m * c1) / (sqrt(v * c2) + eps) -> out / out2 as a bf16 hi/lo pair
 };
 
 // Round an fp32 value to tf32 (10 explicit mantissa bits, nearest, ties away
@@ -84,6 +87,9 @@ struct GroupDesc {
   float alpha, beta;
   int tma_out;  // epilogue stages 32x32 chunks in smem and stores them with TMA (mapOut)
   void* out2;   // second output of the split epilogues (same layout as out)
+  float* st_m;  // EPI_SOAP_ADAM: first / second moments (fp32, same layout as out)
+  float* st_v;
+  float b1, b2, c1, c2, eps;  // EPI_SOAP_ADAM scalars (c1, c2: bias corrections 1/(1-b^t))
 };
 
 struct GemmParams {
@@ -197,7 +203,27 @@ __device__ __forceinline__ void epilogue_chunk(const GroupDesc& G, int b, int ro
   const int lo = G.tri ? max(0, row - col0) : 0;
   if (lo >= ncols) return;
 
-  if constexpr (EPI == EPI_SPLIT_BF16X2 || EPI == EPI_SPLIT_TF32) {
+  if constexpr (EPI == EPI_SOAP_ADAM) {
+    const long long rowoff = (long long)b * G.out_bs + (long long)row * G.ldo + col0;
+    float* pm = G.st_m + rowoff;
+    float* pv = G.st_v + rowoff;
+    __nv_bfloat16* ph = reinterpret_cast<__nv_bfloat16*>(G.out) + rowoff;
+    __nv_bfloat16* pl = reinterpret_cast<__nv_bfloat16*>(G.out2) + rowoff;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j >= ncols) continue;
+      const float g = v[j];
+      const float mm = fmaf(G.b1, pm[j], (1.f - G.b1) * g);
+      const float vv = fmaf(G.b2, pv[j], (1.f - G.b2) * g * g);
+      pm[j] = mm;
+      pv[j] = vv;
+      const float u = (mm * G.c1) / (sqrtf(vv * G.c2) + G.eps);
+      const __nv_bfloat16 h = __float2bfloat16_rn(u);
+      ph[j] = h;
+      pl[j] = __float2bfloat16_rn(u - __bfloat162float(h));
+    }
+    return;
+  } else if constexpr (EPI == EPI_SPLIT_BF16X2 || EPI == EPI_SPLIT_TF32) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       if (j >= ncols) continue;

@@ -204,6 +204,9 @@ size_t lsr_kron_apply_workspace_bytes(int batch, int m, int n, int nterms, int f
          256;
 }
 
+}  // extern "C"
+
+namespace lsr {
 namespace {
 
 // Fill one GEMM group from a list of (A operand, B operand) pairs.
@@ -230,14 +233,19 @@ void set_out(GroupDesc& G, int batch, int m, int n, void* out, void* out2, int o
   G.alpha = 1.f;
 }
 
+}  // namespace
+
 // One term, bf16 operands: Y (+)= A X B^T with the cheaper association first;
 // the intermediate is a bf16 hi + lo pair (two K segments in the second GEMM).
 //   right-first (n > m): U = X B^T -> Y = A U   (U read MN-major)
 //   left-first          : T = A X  -> Y = T B^T (X read MN-major)
+// fac_batched = 1: A and B hold one factor per batch entry ([batch][m][m], [batch][n][n]).
 int kron_term_bf16(const void* A, int a_trans, const void* X, const void* B, float* Y, void* Th, void* Tl, int batch,
-                   int m, int n, int accumulate, cudaStream_t st) {
+                   int m, int n, int accumulate, cudaStream_t st, int fac_batched) {
   const bool right_first = n > m;
-  const Operand Aop = mat(A, m, m, 1, a_trans ? 1 : 0, 0);  // A[r][k], or A^T stored [k][r]
+  const int fb = fac_batched ? batch : 1;
+  const int bc = fac_batched ? 0 : 1;  // broadcast flag of the factors
+  const Operand Aop = mat(A, m, m, fb, a_trans ? 1 : 0, 0);  // A[r][k], or A^T stored [k][r]
   const int am = a_trans ? 1 : 0;
   {
     GemmParams p{};
@@ -245,12 +253,12 @@ int kron_term_bf16(const void* A, int a_trans, const void* X, const void* B, flo
     set_out(p.g[0], batch, m, n, Th, Tl, 0);
     int rc;
     if (right_first) {
-      const Operand pr[1][2] = {{mat(X, m, n, batch, 0, 0), mat(B, n, n, 1, 0, 0)}};
-      const SegDesc sg[1] = {SegDesc{cdiv(n, BK), 0, 0, 0, 1}};
+      const Operand pr[1][2] = {{mat(X, m, n, batch, 0, 0), mat(B, n, n, fb, 0, 0)}};
+      const SegDesc sg[1] = {SegDesc{cdiv(n, BK), 0, 0, 0, bc}};
       rc = set_segments(p, pr, sg, 1);
     } else {
       const Operand pr[1][2] = {{Aop, mat(X, m, n, batch, 1, 0)}};
-      const SegDesc sg[1] = {SegDesc{cdiv(m, BK), am, 1, 1, 0}};
+      const SegDesc sg[1] = {SegDesc{cdiv(m, BK), am, 1, bc, 0}};
       rc = set_segments(p, pr, sg, 1);
     }
     if (!rc) rc = launch_gemm<K_BN, EPI_SPLIT_BF16X2>(p, st);
@@ -267,16 +275,18 @@ int kron_term_bf16(const void* A, int a_trans, const void* X, const void* B, flo
   int rc;
   if (right_first) {
     const Operand pr[2][2] = {{Aop, mat(Th, m, n, batch, 1, 0)}, {Aop, mat(Tl, m, n, batch, 1, 0)}};
-    const SegDesc sg[2] = {SegDesc{cdiv(m, BK), am, 1, 1, 0}, SegDesc{cdiv(m, BK), am, 1, 1, 0}};
+    const SegDesc sg[2] = {SegDesc{cdiv(m, BK), am, 1, bc, 0}, SegDesc{cdiv(m, BK), am, 1, bc, 0}};
     rc = set_segments(p, pr, sg, 2);
   } else {
-    const Operand pr[2][2] = {{mat(Th, m, n, batch, 0, 0), mat(B, n, n, 1, 0, 0)},
-                              {mat(Tl, m, n, batch, 0, 0), mat(B, n, n, 1, 0, 0)}};
-    const SegDesc sg[2] = {SegDesc{cdiv(n, BK), 0, 0, 0, 1}, SegDesc{cdiv(n, BK), 0, 0, 0, 1}};
+    const Operand pr[2][2] = {{mat(Th, m, n, batch, 0, 0), mat(B, n, n, fb, 0, 0)},
+                              {mat(Tl, m, n, batch, 0, 0), mat(B, n, n, fb, 0, 0)}};
+    const SegDesc sg[2] = {SegDesc{cdiv(n, BK), 0, 0, 0, bc}, SegDesc{cdiv(n, BK), 0, 0, 0, bc}};
     rc = set_segments(p, pr, sg, 2);
   }
   return rc ? rc : launch_gemm<K_BN, EPI_F32_EMA>(p, st);
 }
+
+namespace {
 
 // One term, fp32 operands as tf32 hi/lo pairs (3xTF32), every operand K-major:
 //   right-first: U = X B^T, stored transposed (U^T, [n][m]) as a tf32 pair -> Y = A U
@@ -353,7 +363,7 @@ int kron_apply(const void* A, int a_trans, const void* X, const void* B, float* 
     for (int s = 0; s < nterms && !rc; ++s) {
       const void* As = static_cast<const uint8_t*>(A) + (size_t)s * m * m * 2;
       const void* Bs = static_cast<const uint8_t*>(B) + (size_t)s * n * n * 2;
-      rc = kron_term_bf16(As, a_trans, X, Bs, Y, Th, Tl, batch, m, n, s > 0, st);
+      rc = kron_term_bf16(As, a_trans, X, Bs, Y, Th, Tl, batch, m, n, s > 0, st, 0);
     }
     return rc;
   }
@@ -380,6 +390,9 @@ int kron_apply(const void* A, int a_trans, const void* X, const void* B, float* 
 }
 
 }  // namespace
+}  // namespace lsr
+
+extern "C" {
 
 int lsr_kron_apply_bf16(const void* A, int a_trans, const void* X, const void* B, float* Y, int batch, int m, int n,
                         int nterms, void* ws, size_t ws_bytes, lsr_stream_t stream) {

@@ -107,6 +107,7 @@ inline void setup_out_map(GemmParams& p, int g) {
   using T = EpiT<EPI>;
   GroupDesc& G = p.g[g];
   G.tma_out = 0;
+  if (EPI == EPI_SOAP_ADAM) return;  // reads and writes four arrays: direct-store epilogue
   auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   if (!G.out || !a16(G.out) || (G.ldo * T::ESZ) % 16 || (G.out_bs * T::ESZ) % 16 || G.N % T::EPV) return;
   if (T::AUX && (!G.aux || !a16(G.aux) || (G.ld_aux * T::ESZ) % 16 || (G.aux_bs * T::ESZ) % 16)) return;
@@ -146,5 +147,10 @@ inline int launch_gemm(GemmParams& p, cudaStream_t st, int kind = PK_GEMM_OTHER)
   kfn<<<grid, kGemmThreads, L::TOTAL, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? LSR_OK : LSR_ERR_LAUNCH;
 }
+
+// One Kronecker-apply term with bf16 operands, Y (+)= A X B^T over a batch
+// (kron.cu); Th/Tl: bf16 scratch for the hi/lo intermediate, batch*m*n each.
+int kron_term_bf16(const void* A, int a_trans, const void* X, const void* B, float* Y, void* Th, void* Tl, int batch,
+                   int m, int n, int accumulate, cudaStream_t st, int fac_batched);
 
 }  // namespace lsr

@@ -77,6 +77,18 @@ SIGNATURES: dict[str, tuple] = {
     "lsr_kron_apply_f32": (
         c_int,
         [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "lsr_soap_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "lsr_soap_direction_bf16": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+         c_float, c_float, c_float, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "lsr_shampoo_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "lsr_shampoo_direction_bf16": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_int, c_void_p,
+         c_size_t, c_void_p]),
+    "lsr_blocks_gather_bf16": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "lsr_blocks_apply_bf16": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_float, c_float, c_void_p]),
     "lsr_muon_workspace_bytes": (c_size_t, [ctypes.POINTER(MuonGroup), c_int]),
     "lsr_muon_step_bf16": (
         c_int,

@@ -215,6 +215,47 @@ LSR_API int lsr_kron_apply_bf16(const void* A, int a_trans, const void* X, const
 LSR_API int lsr_kron_apply_f32(const float* A, int a_trans, const float* X, const float* B, float* Y, int batch,
                                int m, int n, int nterms, void* ws, size_t ws_bytes, lsr_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Shampoo / SOAP on stacks of equally shaped parameter blocks
+ * ([batch][rows][cols], blocks of at most max_preconditioner_dim per side).
+ *
+ * Replaces the preconditioner math of DistributedShampoo (third-party
+ * distributed_shampoo; constructed in shampoo_soap_lm_ddp_zero1.py:312-400,
+ * stepped at :609) for the "shampoo" (Adam grafting) and "soap"
+ * (DefaultSOAPConfig) modes. bf16 operands, fp32 accumulation and state.
+ *
+ * lsr_soap_direction_bf16: with update_stats, first
+ *     L = beta2 L + (1-beta2) G G^T,  R = beta2 R + (1-beta2) G^T G;
+ *   then G' = Q_L^T G Q_R and Adam in that basis (fused into the rotation):
+ *     m = beta1 m + (1-beta1) G',  v = beta2 v + (1-beta2) G'^2,
+ *     U' = (m / (1-beta1^step)) / (sqrt(v / (1-beta2^step)) + eps),
+ *   and the update direction U = Q_L U' Q_R^T (fp32).
+ *   L fp32 [b][r][r], R fp32 [b][c][c], Q_L bf16 [b][r][r], Q_R bf16 [b][c][c],
+ *   m, v fp32 [b][r][c]; rows, cols multiples of 8.
+ * lsr_shampoo_direction_bf16: optional statistics update as above, then
+ *   P = Lroot G Rroot with precomputed bf16 inverse roots Lroot = L^{-1/4},
+ *   Rroot = R^{-1/4} (symmetric), one pair per block; P fp32.
+ * ---------------------------------------------------------------------- */
+LSR_API size_t lsr_soap_workspace_bytes(int batch, int rows, int cols);
+LSR_API int lsr_soap_direction_bf16(const void* G, float* L, float* R, const void* QL, const void* QR, float* m,
+                                    float* v, float* U, int batch, int rows, int cols, float beta1, float beta2,
+                                    float eps, int step, int update_stats, void* ws, size_t ws_bytes,
+                                    lsr_stream_t stream);
+LSR_API size_t lsr_shampoo_workspace_bytes(int batch, int rows, int cols);
+LSR_API int lsr_shampoo_direction_bf16(const void* G, float* L, float* R, const void* Lroot, const void* Rroot,
+                                       float* P, int batch, int rows, int cols, float beta2, int update_stats,
+                                       void* ws, size_t ws_bytes, lsr_stream_t stream);
+
+/* Parameter blocks: ptrs / lds are DEVICE arrays of `nblocks` bf16 block
+ * addresses (element (0,0) of the block inside its parameter) and parameter
+ * row strides. Gather copies the blocks into stack [nblocks][rows][cols];
+ * apply performs the decoupled update p = p (1 - lr wd) - lr U per block
+ * (WeightDecayType.DECOUPLED, shampoo_soap_lm_ddp_zero1.py:340). */
+LSR_API int lsr_blocks_gather_bf16(const uint64_t* ptrs, const int* lds, int nblocks, int rows, int cols,
+                                   void* stack, lsr_stream_t stream);
+LSR_API int lsr_blocks_apply_bf16(const uint64_t* ptrs, const int* lds, int nblocks, int rows, int cols,
+                                  const float* U, float lr, float weight_decay, lsr_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

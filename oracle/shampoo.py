@@ -1,0 +1,96 @@
+"""CPU restatement of the Shampoo / SOAP preconditioner math (oracle / test infrastructure only).
+
+PARITY UNPINNED: the reference takes this math from the third-party
+``distributed_shampoo`` package (facebookresearch/optimizers, installed from
+git HEAD without a pinned version, shampoo_soap_lm_ddp_zero1.py:31-36; used at
+:132-168, :312-400, :609), which is absent here and has no golden vectors in
+the reference. This module restates the published formulas of the workload
+definition and reuses the reference's own in-repo pieces:
+
+* two-sided product ``A X B^T``       — kron_apply_shared_2d, hft.py:108-140
+* inverse p-th roots                  — coupled_newton_one, shampoo.py:277-347
+                                        (and an fp64 eigendecomposition for precomputed roots)
+
+Formulas (per block G of at most max_preconditioner_dim per side):
+  statistics  L = b2 L + (1-b2) G G^T,   R = b2 R + (1-b2) G^T G
+  Shampoo     P = L^{-1/4} G R^{-1/4}
+  SOAP        G' = Q_L^T G Q_R; m = b1 m + (1-b1) G'; v = b2 v + (1-b2) G'^2;
+              U' = (m/(1-b1^t)) / (sqrt(v/(1-b2^t)) + eps);  U = Q_L U' Q_R^T
+Arithmetic in float64 on the given (bf16-valued) operands.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def stats_update(L, R, G, beta2):
+    G = np.asarray(G, np.float64)
+    Gt = np.swapaxes(G, -1, -2)
+    L = beta2 * np.asarray(L, np.float64) + (1.0 - beta2) * (G @ Gt)
+    R = beta2 * np.asarray(R, np.float64) + (1.0 - beta2) * (Gt @ G)
+    return L, R
+
+
+def inverse_root(S, root: int = 4, eps: float = 0.0):
+    """(S + eps I)^{-1/root} of a symmetric positive (semi)definite matrix via fp64 eigh."""
+    S = np.asarray(S, np.float64)
+    n = S.shape[-1]
+    w, V = np.linalg.eigh(S + eps * np.eye(n))
+    w = np.maximum(w, 1e-300)
+    return (V * w[..., None, :] ** (-1.0 / root)) @ np.swapaxes(V, -1, -2)
+
+
+def shampoo_precondition(G, Lroot, Rroot):
+    return np.asarray(Lroot, np.float64) @ np.asarray(G, np.float64) @ np.asarray(Rroot, np.float64)
+
+
+def soap_direction(G, QL, QR, m, v, beta1, beta2, eps, step):
+    """Returns (U, m, v) for one SOAP step in the eigenbases QL, QR."""
+    QL = np.asarray(QL, np.float64)
+    QR = np.asarray(QR, np.float64)
+    Gr = np.swapaxes(QL, -1, -2) @ np.asarray(G, np.float64) @ QR
+    m = beta1 * np.asarray(m, np.float64) + (1.0 - beta1) * Gr
+    v = beta2 * np.asarray(v, np.float64) + (1.0 - beta2) * Gr * Gr
+    Up = (m / (1.0 - beta1 ** step)) / (np.sqrt(v / (1.0 - beta2 ** step)) + eps)
+    U = QL @ Up @ np.swapaxes(QR, -1, -2)
+    return U, m, v
+
+
+def coupled_newton_one(A, root, epsilon=0.0, tolerance=1e-6, max_iterations=100):
+    """Coupled Newton iteration for A^{-1/root}, restated from shampoo.py:277-347.
+
+    X_0 = z^{1/root} I, M_0 = z A with z = (root+1) / (2 ||A||_F); repeat
+    Mp = (1 - 1/root) I + M/root ... in the reference's form Mp = alpha M + (1-alpha) I
+    with alpha = -1/root; X <- X Mp; M <- Mp^root M; until max|M - I| <= tolerance.
+    Returns (X, iterations, error).
+    """
+    A = np.asarray(A, np.float64)
+    n = A.shape[0]
+    I = np.eye(n)
+    Ar = A + epsilon * I if epsilon != 0.0 else A
+    alpha = -1.0 / float(root)
+    z = (root + 1.0) / (2.0 * np.linalg.norm(Ar))
+    X = z ** (-alpha) * I
+    M = z * Ar
+    err = np.abs(M - I).max()
+    it = 0
+    while err > tolerance and it < max_iterations:
+        Mp = alpha * M + (1.0 - alpha) * I
+        X = X @ Mp
+        M = np.linalg.matrix_power(Mp, root) @ M
+        err = np.abs(M - I).max()
+        it += 1
+    return X, it, float(err)
+
+
+def block_sizes(n: int, max_dim: int) -> list[int]:
+    """Split a dimension into blocks of max_dim plus a remainder (1600 -> [1024, 576])."""
+    out = [max_dim] * (n // max_dim)
+    if n % max_dim:
+        out.append(n % max_dim)
+    return out
+
+
+def soap_flops(r: int, c: int) -> float:
+    """Algorithmic flops of one SOAP block step: stats 2r^2c + 2rc^2, rotate and rotate back 2 x (2r^2c + 2rc^2)."""
+    return 6.0 * r * c * (r + c)

@@ -99,3 +99,16 @@ def test_product_path_has_no_cpu_fallback():
         lsr.zeropower_serial(torch.zeros(8, 8, dtype=torch.bfloat16), 5, 1e-7)
     src = "".join(p.read_text() for p in (ROOT / "cuda-lsr_b200" / "lsr").glob("*.py"))
     assert "oracle" not in src
+
+
+def test_shampoo_block_partition_and_owners():
+    from lsr.shampoo import assign_owners, param_blocks
+    blocks = param_blocks((1600, 4800), 1024)
+    assert len(blocks) == 10
+    assert blocks[0] == (0, 0, 1024, 1024) and blocks[-1] == (1024, 4096, 576, 704)
+    costs = [6.0 * r * c * (r + c) for _, _, r, c in blocks]
+    for world in (1, 2, 4, 8):
+        own = assign_owners(costs, world)
+        loads = [sum(cc for cc, o in zip(costs, own) if o == k) for k in range(world)]
+        assert set(own) <= set(range(world))
+        assert max(loads) <= sum(costs) / world + max(costs)

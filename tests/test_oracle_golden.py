@@ -116,3 +116,35 @@ def test_kron_oracle_matches_reference_golden():
         W = ok.dense_operator(A, B)
         Yd = (X.reshape(X.shape[0], -1).astype(np.float64) @ W.T).reshape(X.shape)
         assert rel_fro(Yd, z[f"multi{S}_Ydense"]) < 1e-6
+
+
+# ---------------------------------------------------------------- Shampoo oracle
+def test_coupled_newton_matches_reference_golden():
+    from oracle import shampoo as osh
+    z = np.load(GOLD / "newton_golden.npz")
+    for i in range(2):
+        A = z[f"newton{i}_A"]
+        for root in (2, 4):
+            X, it, err = osh.coupled_newton_one(A, root)
+            assert rel_fro(X, z[f"newton{i}_root{root}"]) < 1e-4
+            # and it is the inverse root
+            assert rel_fro(np.linalg.matrix_power(X, root) @ A, np.eye(A.shape[0])) < 1e-4
+            assert rel_fro(X, osh.inverse_root(A, root)) < 1e-4
+
+
+def test_gpt2xl_soap_blocks():
+    """Config 5's blocking: 42 blocks per layer, 2016 in total, the survey's shape counts."""
+    import collections
+    from oracle import shampoo as osh
+    assert osh.block_sizes(1600, 1024) == [1024, 576]
+    assert osh.block_sizes(4800, 1024) == [1024] * 4 + [704]
+    assert osh.block_sizes(6400, 1024) == [1024] * 6 + [256]
+    cnt = collections.Counter()
+    for r, c in [(1600, 4800), (1600, 1600), (1600, 6400), (6400, 1600)]:
+        for rb in osh.block_sizes(r, 1024):
+            for cb in osh.block_sizes(c, 1024):
+                cnt[(rb, cb)] += 1
+    assert sum(cnt.values()) == 42
+    assert cnt[(1024, 1024)] == 17 and cnt[(576, 1024)] == 11 and cnt[(1024, 576)] == 7
+    total = 48 * sum(osh.soap_flops(r, c) * k for (r, c), k in cnt.items())
+    assert abs(total / 1e12 - 16.29) < 0.01
