@@ -245,7 +245,8 @@ def run_lsr(args) -> None:
             opt.momentum[p].copy_(m)
         step = opt.muon_step
     else:
-        opt = ShardedMuon(params, lr=LR, momentum=MU, nesterov=True, weight_decay=WD, ns_steps=NS_STEPS, eps=EPS)
+        opt = ShardedMuon(params, lr=LR, momentum=MU, nesterov=True, weight_decay=WD, ns_steps=NS_STEPS, eps=EPS,
+                          flat_params=True)
         for Gp in opt.groups:
             for k, j in enumerate(Gp.owned):
                 idx = next(i for i, p in enumerate(params) if p is Gp.params[j])
@@ -307,8 +308,9 @@ def run_lsr(args) -> None:
         "dense_flops_per_launch": flops_per_launch, "avg_launch_ms": round(dom_avg_ms, 4),
         "step": {"dense_tflop": round(step_flops / 1e12, 3),
                  "achieved_tflops": round(step_flops / (ms * 1e-3) / 1e12, 1),
-                 "frac_of_sustained": round(step_flops / (ms * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"], 4),
-                 "frac_of_burst": round(step_flops / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4)},
+                 "per_gpu_frac_of_sustained": round(
+                     step_flops / (ms * 1e-3) / 1e12 / world / peaks["bf16_tflops_sustained"], 4),
+                 "per_gpu_frac_of_burst": round(step_flops / (ms * 1e-3) / 1e12 / world / peaks["bf16_tflops"], 4)},
         "per_kind_ms_per_step": {k: round(v[0] / args.steps, 3) for k, v in prof.items() if v[1]},
     }
 

@@ -53,6 +53,8 @@ class ShardGroup:
     momentum: list = field(default_factory=list)  # momentum buffers of the owned matrices
     local_buf: torch.Tensor | None = None   # [per, m, n] oriented updates of this rank
     gather_buf: torch.Tensor | None = None  # [world * per, m, n]
+    flat_buf: torch.Tensor | None = None    # flat mode: parameters, rank-major [world * per, r, c]
+    own_slice: torch.Tensor | None = None   # flat mode: this rank's slots of flat_buf
 
 
 class ShardedMuon:
@@ -60,10 +62,17 @@ class ShardedMuon:
 
     params: list of 2-D bf16 CUDA parameters (all ranks pass the same list in
     the same order). Gradients are read from ``p.grad`` of the owned matrices.
+
+    flat_params=True re-homes each shape group's parameters into one
+    rank-major buffer (``p.data`` becomes a view of it, like a flat-parameter
+    ZeRO layout): each rank then applies only its own updates and the updated
+    parameters are all-gathered in place, so no rank applies another rank's
+    updates. flat_params=False keeps the caller's storage: the oriented
+    updates are all-gathered and every rank applies all of them.
     """
 
     def __init__(self, params, lr=0.02, momentum=0.95, nesterov=True, weight_decay=0.01, ns_steps=5, eps=1e-7,
-                 lr_adjust="original", process_group=None, engine=None, overlap=True):
+                 lr_adjust="original", process_group=None, engine=None, overlap=True, flat_params=False):
         self.lr, self.mu, self.nesterov, self.wd = lr, momentum, nesterov, weight_decay
         self.ns_steps, self.eps, self.lr_adjust = ns_steps, eps, lr_adjust
         self.pg = process_group
@@ -89,7 +98,20 @@ class ShardedMuon:
             G.local_buf = torch.zeros(per, m, n, dtype=torch.bfloat16, device=dev)
             G.gather_buf = torch.zeros(self.world * per, m, n, dtype=torch.bfloat16, device=dev) \
                 if self.world > 1 else G.local_buf
-        self.comm_stream = torch.cuda.Stream() if (self.world > 1 and torch.cuda.is_available()) else None
+        on_gpu = all(p.is_cuda for G in self.groups for p in G.params)
+        self.comm_stream = torch.cuda.Stream() if (self.world > 1 and on_gpu) else None
+        self.flat = bool(flat_params) and self.world > 1
+        if self.flat:
+            for G in self.groups:
+                order = gathered_order(len(G.params), self.world)
+                p0 = G.params[0]
+                G.flat_buf = torch.zeros((len(order),) + tuple(G.shape), dtype=p0.dtype, device=p0.device)
+                for k, j in enumerate(order):
+                    if j is not None:
+                        G.flat_buf[k].copy_(G.params[j].data)
+                        G.params[j].data = G.flat_buf[k]
+                per = local_count(len(G.params), self.world)
+                G.own_slice = G.flat_buf[self.rank * per:(self.rank + 1) * per]
 
     def state_dict(self):
         return {"momentum": [[b for b in G.momentum] for G in self.groups], "rank": self.rank, "world": self.world}
@@ -121,26 +143,57 @@ class ShardedMuon:
             upd = G.gather_buf[torch.tensor(slots, device=G.gather_buf.device)].contiguous()
         self.engine.apply([(G.shape, G.lr, items)], [upd], weight_decay=self.wd, base_lr=self.lr)
 
+    def _apply_own(self, G: ShardGroup) -> None:
+        """Flat mode: apply this rank's updates to its own parameters (in the flat buffer)."""
+        if not G.owned:
+            return
+        items = [(G.params[j], None, None, G.lr) for j in G.owned]
+        self.engine.apply([(G.shape, G.lr, items)], [G.local_buf[:len(items)]], weight_decay=self.wd,
+                          base_lr=self.lr)
+
+    def _step_flat(self) -> None:
+        if self.comm_stream is None or not self.overlap:
+            for G in self.groups:
+                self._orthogonalize(G)
+                self._apply_own(G)
+                dist.all_gather_into_tensor(G.flat_buf, G.own_slice, group=self.pg)
+            return
+        compute = torch.cuda.current_stream()
+        comm = self.comm_stream
+        for G in self.groups:
+            self._orthogonalize(G)
+            self._apply_own(G)
+            ev = torch.cuda.Event()
+            ev.record(compute)
+            comm.wait_event(ev)
+            with torch.cuda.stream(comm):
+                dist.all_gather_into_tensor(G.flat_buf, G.own_slice, group=self.pg)
+        compute.wait_stream(comm)
+
     @torch.no_grad()
     def step(self) -> None:
+        if self.flat:
+            self._step_flat()
+            return
         if self.world == 1:
             for G in self.groups:
                 self._orthogonalize(G)
+                self._apply(G)
+            return
+        if self.comm_stream is None or not self.overlap:
+            for G in self.groups:
+                self._orthogonalize(G)
+                dist.all_gather_into_tensor(G.gather_buf, G.local_buf, group=self.pg)
                 self._apply(G)
             return
         compute = torch.cuda.current_stream()
         comm = self.comm_stream
         for G in self.groups:
             self._orthogonalize(G)
-            if self.overlap:
-                ev = torch.cuda.Event()
-                ev.record(compute)
-                comm.wait_event(ev)
-                with torch.cuda.stream(comm):
-                    dist.all_gather_into_tensor(G.gather_buf, G.local_buf, group=self.pg)
-                    self._apply(G)
-            else:
+            ev = torch.cuda.Event()
+            ev.record(compute)
+            comm.wait_event(ev)
+            with torch.cuda.stream(comm):
                 dist.all_gather_into_tensor(G.gather_buf, G.local_buf, group=self.pg)
                 self._apply(G)
-        if self.overlap:
-            compute.wait_stream(comm)
+        compute.wait_stream(comm)
