@@ -297,7 +297,9 @@ def run_lsr(args) -> None:
     dom_avg_ms = dom_ms / max(dom_n, 1)
     achieved = flops_per_launch / (dom_avg_ms * 1e-3) / 1e12 if dom_n else None
     step_flops = sum(ns_dense_flops(s) for s in shapes)
-    traffic = load_traffic(dom)
+    traffic = load_traffic(dom)  # bytes of the full 192-matrix launch; scale to this launch's share
+    if traffic is not None:
+        traffic = round(traffic * flops_per_launch / phase_flops([s for _ in range(N_LAYERS) for s in LAYER_SHAPES])[dom])
     roofline = {
         "bound": "tensor", "kernel": f"gemm_sm100_kernel ({dom})",
         "achieved": round(achieved, 1) if achieved else None,
@@ -383,13 +385,14 @@ def run_e2e(args, params, grads, step, world, opt):
 
 def load_traffic(kind: str):
     """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if present."""
-    f = ROOT / "profiles" / "traffic.json"
+    f = ROOT / "profiles" / "traffic_per_launch.txt"
     if not f.exists():
         return None
-    try:
-        return json.loads(f.read_text()).get(kind)
-    except Exception:
-        return None
+    for line in f.read_text().splitlines():
+        parts = line.split()
+        if len(parts) == 2 and not line.startswith("#") and parts[0] == kind:
+            return float(parts[1])
+    return None
 
 
 def main(argv=None) -> int:
