@@ -395,6 +395,140 @@ def load_traffic(kind: str):
     return None
 
 
+# ---------------------------------------------------------------------------
+# Per-row workloads (not the headline line): --workload cfg1|cfg2|cfg3|cfg5
+# ---------------------------------------------------------------------------
+
+def _time_gpu(fn, warmup, iters, flush_bytes=256 << 20):
+    """Mean ms of fn() over `iters` runs, L2 flushed (a buffer larger than L2 is written) before each."""
+    flush = torch.empty(flush_bytes, dtype=torch.uint8, device="cuda")
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(iters):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        tot += a.elapsed_time(b)
+    return tot / iters
+
+
+def _time_cpu(fn, reps=2):
+    fn()
+    t = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        fn()
+        t.append((time.perf_counter() - t0) * 1e3)
+    return statistics.median(t)
+
+
+def run_workload(args) -> None:
+    import lsr
+    import lsr.kron as K
+    from lsr import shampoo as SH
+    torch.cuda.set_device(0)
+    peaks = measured_peaks()
+    dev = torch.device("cuda", 0)
+    lines = []
+    w = args.workload
+    if w == "cfg1":
+        g = torch.Generator().manual_seed(0)
+        wide = (torch.randn(12, 768, 3072, generator=g) * 0.02).bfloat16().to(dev)
+        tall = (torch.randn(12, 3072, 768, generator=g) * 0.02).bfloat16().to(dev)
+        ms = _time_gpu(lambda: (lsr.zeropower_via_newtonschulz5(wide, 5, 1e-7),
+                                lsr.zeropower_via_newtonschulz5(tall, 5, 1e-7)), args.warmup, args.steps)
+        fl = 24 * ns_dense_flops((768, 3072))
+        from oracle import muon as om
+        G1 = wide[0].float().cpu().numpy()
+        cpu = _time_cpu(lambda: om.zeropower(G1, 5, 1e-7), 1) * 24
+        lines.append({"workload": "cfg1: Newton-Schulz, 12x(768x3072) + 12x(3072x768), 5 steps", "value": ms,
+                      "unit": "ms", "dense_tflop": fl / 1e12, "tflops": fl / ms / 1e9,
+                      "frac_of_sustained": fl / ms / 1e9 / peaks["bf16_tflops_sustained"],
+                      "cpu_ms": cpu, "cpu_sample": "1 matrix via the numpy restatement, x24"})
+    elif w == "cfg2":
+        g = torch.Generator().manual_seed(1)
+        Ms = [torch.randn(1024, 1024, generator=g) / 32.0 for _ in range(2)]
+        A, B = [((m + m.T) / 2).contiguous().to(dev) for m in Ms]
+        X = torch.randn(64, 1024, 1024, generator=torch.Generator().manual_seed(2)).to(dev)
+        fl = 64 * (2.0 * 1024 ** 3 * 2)
+        for name, a, x, b, peak in (("fp32 (3xTF32)", A, X, B, peaks["bf16_tflops_sustained"] / 2),
+                                    ("bf16", A.bfloat16(), X.bfloat16(), B.bfloat16(),
+                                     peaks["bf16_tflops_sustained"])):
+            Y = torch.empty(64, 1024, 1024, device=dev)
+            ms = _time_gpu(lambda: K.kron_sum(a, x, b, out=Y), args.warmup, args.steps)
+            nbytes = x.numel() * x.element_size() + Y.numel() * 4
+            line = {"workload": f"cfg2: Kronecker sum (A+B)vec(X), A,B 1024^2, 64 RHS, {name}", "value": ms,
+                    "unit": "ms", "algorithmic_gflop": fl / 1e9, "tflops": fl / ms / 1e9,
+                    "min_bytes": nbytes, "gbs": nbytes / ms / 1e6}
+            if name.startswith("fp32"):
+                line["tensor_tflops_3xtf32"] = 3 * fl / ms / 1e9
+                line["note"] = "3 tf32 products per fp32 product; tf32 dense peak is half the bf16 peak"
+                line["frac_of_tf32_peak_3x"] = 3 * fl / ms / 1e9 / peak
+            else:
+                line["frac_of_sustained"] = fl / ms / 1e9 / peak
+            lines.append(line)
+        An, Bn, Xn = A.cpu().numpy(), B.cpu().numpy(), X[:4].cpu().numpy()
+        cpu = _time_cpu(lambda: An @ Xn + Xn @ Bn.T, 2) * 16
+        lines[0]["cpu_ms"] = cpu
+        lines[0]["cpu_sample"] = "4 of 64 right-hand sides, numpy fp32 A@X + X@B.T, x16"
+    elif w in ("cfg3", "cfg5"):
+        g = torch.Generator().manual_seed(3 if w == "cfg3" else 5)
+
+        gq = torch.Generator(device=dev).manual_seed(3 if w == "cfg3" else 5)
+
+        def orth(n, b):  # seeded random orthogonal bases: QR of N(0, 1)
+            return torch.linalg.qr(torch.randn(b, n, n, generator=gq, device=dev))[0].bfloat16().contiguous()
+        if w == "cfg3":
+            r, c = 1600, 6400
+            G = (torch.randn(1, r, c, generator=g) * 0.01).bfloat16().to(dev)
+            L = torch.zeros(1, r, r, device=dev)
+            R = torch.zeros(1, c, c, device=dev)
+            ms_stats = _time_gpu(lambda: (SH.gram_update(G, L, 0, 0.0, 1.0), SH.gram_update(G, R, 1, 0.0, 1.0)),
+                                 args.warmup, args.steps)
+            Lr, Rr = orth(r, 1), orth(c, 1)  # stand-ins with the shapes of the precomputed inverse roots
+            ms_apply = _time_gpu(lambda: SH.shampoo_direction(G, Lr, Rr), args.warmup, args.steps)
+            m = torch.zeros(1, r, c, device=dev)
+            v = torch.zeros(1, r, c, device=dev)
+            ms_soap = _time_gpu(lambda: SH.soap_direction(G, None, None, Lr, Rr, m, v, 0.95, 0.95, 1e-8, 1, False),
+                                args.warmup, args.steps)
+            f_stats = 2.0 * r * r * c + 2.0 * r * c * c
+            for name, ms, fl in (("statistics L=GG^T, R=G^TG", ms_stats, f_stats),
+                                 ("Shampoo apply L^-1/4 G R^-1/4", ms_apply, f_stats),
+                                 ("SOAP rotate, Adam, rotate back", ms_soap, 2 * f_stats)):
+                lines.append({"workload": f"cfg3: 1600x6400, {name}", "value": ms, "unit": "ms",
+                              "algorithmic_gflop": fl / 1e9, "tflops": fl / ms / 1e9,
+                              "frac_of_sustained": fl / ms / 1e9 / peaks["bf16_tflops_sustained"]})
+        else:
+            shapes = [s for _ in range(args.layers) for s in LAYER_SHAPES]
+            params = [torch.nn.Parameter((torch.randn(*s, generator=g) * 0.02).bfloat16().to(dev)) for s in shapes]
+            for p in params:
+                p.grad = (torch.randn(*p.shape, generator=g) * 0.01).bfloat16().to(dev)
+            opt = SH.DistributedShampoo(params, lr=0.02, betas=(0.95, 0.95), epsilon=1e-8, weight_decay=0.01,
+                                        max_preconditioner_dim=1024, precondition_frequency=10 ** 9,
+                                        start_preconditioning_step=10 ** 9,
+                                        preconditioner_config=SH.DefaultSOAPConfig)
+            opt.step()  # builds the block groups
+            for _, grp, _ in opt._groups:
+                n, r, c = grp.stack.shape
+                grp.QL, grp.QR = orth(r, n), orth(c, n)
+            ms = _time_gpu(opt.step, args.warmup, args.steps)
+            from oracle import shampoo as osh
+            fl = sum(osh.soap_flops(r, c) * len(grp.refs) for (r, c), grp, _ in opt._groups)
+            lines.append({"workload": f"cfg5: GPT-2-XL SOAP step, {args.layers} layers, "
+                                      f"{sum(len(grp.refs) for _, grp, _ in opt._groups)} blocks at 1024, 1 GPU",
+                          "value": ms, "unit": "ms", "algorithmic_tflop": fl / 1e12, "tflops": fl / ms / 1e9,
+                          "frac_of_sustained": fl / ms / 1e9 / peaks["bf16_tflops_sustained"]})
+    for ln in lines:
+        ln.update({"steps": args.steps, "warmup": args.warmup, "l2": "flushed (256 MB write) before each run",
+                   "peak_kind": peaks["source"], "cores": os.cpu_count() or 1})
+        print(json.dumps(ln), flush=True)
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -404,7 +538,12 @@ def main(argv=None) -> int:
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="GPT-2-XL layers (48 = the full model)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["muon", "cfg1", "cfg2", "cfg3", "cfg5"], default="muon",
+                    help="muon = the headline GPT-2-XL Muon step (default); cfgN = per-row workloads")
     args = ap.parse_args(argv)
+    if args.workload != "muon" and args.impl == "lsr":
+        run_workload(args)
+        return 0
     if args.impl == "reference":
         run_reference_arm(args)
         return 0

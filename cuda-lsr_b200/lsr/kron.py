@@ -3,6 +3,7 @@
 * ``kron_sum(A, X, B)``            (A ⊕ B) vec(X) = vec(A X + X B^T), one fused kernel
 * ``kron_apply(X, A, B)``          Σ_s A_s X B_s^T  (A [S,m,m] or [m,m], B [S,n,n] or [n,n])
 * ``kron_apply_shared_2d(X, A, B)`` A X B^T per snapshot            hft.py:108-140
+* ``native_reconstruct(factors, K, out)``  W = Σ_s F_0[s] ⊗ ... ⊗ F_{K-1}[s]   kron_cuda.py:516-583
 * ``kron_sum_out(x, at, b, out)``  out[m] = Σ_s A_s x[m] B_s^T with at[s] = A_s^T,
                                    same checks and errors as hft_fused.py:247-319
                                    (sizes generalised beyond [M,64,8] and S in {1,2,4,8})
@@ -119,3 +120,38 @@ def kron_sum_out(x: torch.Tensor, at: torch.Tensor, b: torch.Tensor, out: torch.
     if S < 1:
         raise RuntimeError(f"Supported S values are >= 1; got {S}")
     _kron_apply(x, at, b, True, out)
+
+
+def native_reconstruct(factors, K, out=None, block=256):
+    """W = Σ_s factors[0][s] ⊗ ... ⊗ factors[K-1][s] (kron_cuda.py:516-583; ``block`` is accepted
+    and ignored). factors: K fp32 CUDA tensors [S, r_k, c_k]; out: [Π r_k, Π c_k] fp32 or None."""
+    import ctypes
+    if len(factors) != K:
+        raise ValueError(K)
+    if not 1 <= K <= 8:
+        raise ValueError(K)
+    S = factors[0].shape[0]
+    rows, cols = [], []
+    for f in factors:
+        _check(f, "factor")
+        if f.dtype != torch.float32 or f.dim() != 3 or f.shape[0] != S:
+            raise RuntimeError("factors must be float32 [S, r, c] with a common S")
+        rows.append(f.shape[1])
+        cols.append(f.shape[2])
+    R = 1
+    C = 1
+    for r, c in zip(rows, cols):
+        R *= r
+        C *= c
+    if out is None:
+        out = torch.empty(R, C, dtype=torch.float32, device=factors[0].device)
+    if out.dtype != torch.float32 or not out.is_contiguous() or out.numel() != R * C:
+        raise RuntimeError(f"out must be a contiguous float32 tensor with {R}x{C} elements")
+    ptrs = (ctypes.c_void_p * K)(*[f.data_ptr() for f in factors])
+    rr = (ctypes.c_int * K)(*rows)
+    cc = (ctypes.c_int * K)(*cols)
+    lib = _lib.load()
+    with torch.cuda.device(out.device):
+        rc = lib.lsr_kron_reconstruct_f32(ptrs, rr, cc, K, S, out.data_ptr(), _lib.stream_handle(out.device))
+    _lib.check(rc, "lsr_kron_reconstruct_f32")
+    return out

@@ -216,6 +216,18 @@ LSR_API int lsr_kron_apply_f32(const float* A, int a_trans, const float* X, cons
                                int m, int n, int nterms, void* ws, size_t ws_bytes, lsr_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Tiny-factor Kronecker reconstruction
+ *   W = sum_{s < S} F_0[s] ⊗ F_1[s] ⊗ ... ⊗ F_{K-1}[s]   (fp32, 1 <= K <= 8)
+ * factors / rows / cols: HOST arrays of K entries; factor k is a DEVICE array
+ * [S][rows[k]][cols[k]]; W is [prod rows][prod cols], row-major, with factor
+ * K-1 the fastest-varying mode (torch.kron order).
+ * Replaces native_reconstruct / direct_k{3,4,5}_kernel (kron_cuda.py:242-583),
+ * generalised from the fixed 16 x 768 K = 3/4/5 layouts to any K <= 8.
+ * ---------------------------------------------------------------------- */
+LSR_API int lsr_kron_reconstruct_f32(const float* const* factors, const int* rows, const int* cols, int K, int S,
+                                     float* W, lsr_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Shampoo / SOAP on stacks of equally shaped parameter blocks
  * ([batch][rows][cols], blocks of at most max_preconditioner_dim per side).
  *

@@ -10,6 +10,8 @@ code on CPU (run in a container where the cuda-lsr checkout is mounted):
                       hft_fused.py:463-509. Both modules assert CUDA at import,
                       so the two function definitions are extracted from the
                       reference source with ``ast`` and executed on CPU tensors.
+* kronrec_golden.npz — batched_kron / vectorized_kron of kron_cuda.py:117-145,
+                      :618-629 on K = 5 / 4 / 3 factor sets (same extraction).
 * newton_golden.npz — coupled_newton_one (+ matrix_power_small) of shampoo.py:254-347
                       (same extraction).
 
@@ -181,10 +183,31 @@ def make_newton(ref: Path) -> dict:
     return out
 
 
+def make_kronrec(ref: Path) -> dict:
+    """Tiny-factor Kronecker reconstruction (kron_cuda.py:117-145, :618-629): K = 5 factors of
+    shapes [S,1,3], [S,2,4] x 4 and the exactly merged K = 4 / K = 3 sets built with the
+    reference's batched_kron; W = vectorized_kron(factors) = sum_s kron(...)."""
+    env = {"torch": torch, "math": math}
+    fns = extract_functions(ref / "kron_cuda.py", ["batched_kron", "vectorized_kron"], env)
+    bk, vk = fns["batched_kron"], fns["vectorized_kron"]
+    out: dict[str, np.ndarray] = {}
+    for S in (1, 7, 64):
+        g = torch.Generator().manual_seed(17 + S)
+        f = [0.5 * torch.randn(S, *shape, generator=g) for shape in [(1, 3), (2, 4), (2, 4), (2, 4), (2, 4)]]
+        g01 = bk(f[0], f[1])
+        g012 = bk(g01, f[2])
+        sets = {5: f, 4: [g01, f[2], f[3], f[4]], 3: [g012, f[3], f[4]]}
+        for K, fs in sets.items():
+            for i, t in enumerate(fs):
+                out[f"S{S}_K{K}_f{i}"] = t.numpy()
+            out[f"S{S}_K{K}_W"] = vk(fs).numpy()
+    return out
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--only", choices=["muon", "kron", "newton"], default=None)
+    ap.add_argument("--only", choices=["muon", "kron", "newton", "kronrec"], default=None)
     args = ap.parse_args()
     ref = Path(args.reference)
     if args.only in (None, "muon"):
@@ -193,6 +216,8 @@ def main() -> int:
         np.savez_compressed(HERE / "kron_golden.npz", **make_kron(ref))
     if args.only in (None, "newton"):
         np.savez_compressed(HERE / "newton_golden.npz", **make_newton(ref))
+    if args.only in (None, "kronrec"):
+        np.savez_compressed(HERE / "kronrec_golden.npz", **make_kronrec(ref))
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
     return 0

@@ -100,3 +100,28 @@ def test_kron_sum_out_errors():
         K.kron_sum_out(x, at, b, torch.zeros(4, 64, 4, device="cuda"))
     with pytest.raises(RuntimeError, match="must be CUDA"):
         K.kron_sum_out(x.cpu(), at, b, torch.zeros_like(x))
+
+
+def test_native_reconstruct_matches_reference_golden():
+    """W = Σ_s F0⊗...⊗F_{K-1} on the reference's K = 5 / 4 / 3 factor sets (kron_cuda.py)."""
+    import lsr.kron as K_
+    z = np.load(Path(__file__).parent / "golden" / "kronrec_golden.npz")
+    for S in (1, 7, 64):
+        outs = {}
+        for K in (5, 4, 3):
+            fs = [torch.from_numpy(z[f"S{S}_K{K}_f{i}"]).cuda() for i in range(K)]
+            outs[K] = K_.native_reconstruct(fs, K, torch.empty(16, 768, device="cuda"))
+            assert rel_fro(outs[K].cpu().numpy(), z[f"S{S}_K{K}_W"]) < TOL_F32
+        # exact-merge identity of the three representations (kron_cuda.py:748-770)
+        assert rel_fro(outs[3].cpu().numpy(), outs[5].cpu().numpy()) < TOL_F32
+        assert rel_fro(outs[4].cpu().numpy(), outs[5].cpu().numpy()) < TOL_F32
+
+
+def test_native_reconstruct_general_shapes():
+    import lsr.kron as K_
+    g = torch.Generator(device="cuda").manual_seed(9)
+    fs = [torch.randn(300, r, c, generator=g, device="cuda") * 0.5 for r, c in [(3, 2), (1, 5), (4, 4), (2, 3)]]
+    W = K_.native_reconstruct(fs, 4)
+    ref = ok.reconstruct([f.cpu().numpy() for f in fs])
+    assert W.shape == ref.shape == (24, 120)
+    assert rel_fro(W.cpu().numpy(), ref) < TOL_F32

@@ -148,3 +148,14 @@ def test_gpt2xl_soap_blocks():
     assert cnt[(1024, 1024)] == 17 and cnt[(576, 1024)] == 11 and cnt[(1024, 576)] == 7
     total = 48 * sum(osh.soap_flops(r, c) * k for (r, c), k in cnt.items())
     assert abs(total / 1e12 - 16.29) < 0.01
+
+
+def test_reconstruct_oracle_matches_reference_golden():
+    from oracle import kron as ok
+    z = np.load(GOLD / "kronrec_golden.npz")
+    for S in (1, 7, 64):
+        for K in (5, 4, 3):
+            fs = [z[f"S{S}_K{K}_f{i}"] for i in range(K)]
+            W = ok.reconstruct(fs)
+            assert W.shape == (16, 768)
+            assert rel_fro(W, z[f"S{S}_K{K}_W"]) < 1e-5
