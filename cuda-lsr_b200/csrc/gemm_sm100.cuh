@@ -44,7 +44,7 @@ enum : int {
   EPI_SPLIT_TF32 = 7,    // out = tf32(acc), out2 = acc - tf32(acc)        (hi/lo fp32 pair)
   EPI_SOAP_ADAM = 8,     // Adam in the rotated basis on g = acc, fp32 moments st_m / st_v:
                          //   m = b1 m + (1-b1) g ; v = b2 v + (1-b2) g^2
-                         //   u = (m * c1) / (sqrt(v * c2) + eps) -> out / out2 as a bf16 hi/lo pair
+                         //   u = (m * c1) / (sqrt(v * c2) + eps) -> out (bf16)
 };
 
 // Round an fp32 value to tf32 (10 explicit mantissa bits, nearest, ties away
@@ -207,8 +207,7 @@ __device__ __forceinline__ void epilogue_chunk(const GroupDesc& G, int b, int ro
     const long long rowoff = (long long)b * G.out_bs + (long long)row * G.ldo + col0;
     float* pm = G.st_m + rowoff;
     float* pv = G.st_v + rowoff;
-    __nv_bfloat16* ph = reinterpret_cast<__nv_bfloat16*>(G.out) + rowoff;
-    __nv_bfloat16* pl = reinterpret_cast<__nv_bfloat16*>(G.out2) + rowoff;
+    __nv_bfloat16* pu = reinterpret_cast<__nv_bfloat16*>(G.out) + rowoff;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       if (j >= ncols) continue;
@@ -217,10 +216,7 @@ __device__ __forceinline__ void epilogue_chunk(const GroupDesc& G, int b, int ro
       const float vv = fmaf(G.b2, pv[j], (1.f - G.b2) * g * g);
       pm[j] = mm;
       pv[j] = vv;
-      const float u = (mm * G.c1) / (sqrtf(vv * G.c2) + G.eps);
-      const __nv_bfloat16 h = __float2bfloat16_rn(u);
-      ph[j] = h;
-      pl[j] = __float2bfloat16_rn(u - __bfloat162float(h));
+      pu[j] = __float2bfloat16_rn((mm * G.c1) / (sqrtf(vv * G.c2) + G.eps));
     }
     return;
   } else if constexpr (EPI == EPI_SPLIT_BF16X2 || EPI == EPI_SPLIT_TF32) {
@@ -312,7 +308,8 @@ __device__ __forceinline__ void epilogue_chunk(const GroupDesc& G, int b, int ro
 
 template <int EPI>
 struct EpiT {
-  static constexpr bool F32 = (EPI == EPI_STORE_F32 || EPI == EPI_F32_EMA || EPI == EPI_SPLIT_TF32);
+  static constexpr bool F32 =
+      (EPI == EPI_STORE_F32 || EPI == EPI_F32_EMA || EPI == EPI_SPLIT_TF32 || EPI == EPI_SOAP_ADAM);
   static constexpr bool SPLIT = (EPI == EPI_SPLIT_BF16X2 || EPI == EPI_SPLIT_TF32);
   static constexpr int ESZ = F32 ? 4 : 2;
   static constexpr int ROWB = 32 * ESZ;  // bytes per staged row
@@ -355,6 +352,42 @@ __device__ __forceinline__ void epilogue_chunk_staged(const GemmParams& p, int g
                                                       const uint4 (&cur)[EpiT<EPI>::VPR], uint8_t* dbuf,
                                                       uint8_t* tbuf) {
   using T = EpiT<EPI>;
+  if constexpr (EPI == EPI_SOAP_ADAM) {
+    // Stage the fp32 accumulator rows, then work row-contiguously: 8 lanes per
+    // row, 16-byte vectors, so m / v / u move in coalesced segments.
+    __syncwarp();  // the previous chunk's reads of dbuf are done
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<uint4*>(dbuf + stg_off<128>(lane, j)) = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+    __syncwarp();
+    const int jv = lane & 7;
+#pragma unroll 2
+    for (int i = 0; i < 8; ++i) {
+      const int rr = (lane >> 3) + 4 * i;
+      const int gr = row0 + rr, gc = col0 + 4 * jv;
+      if (gr >= G.M || gc >= G.N) continue;
+      const float4 g4 = *reinterpret_cast<const float4*>(dbuf + stg_off<128>(rr, jv));
+      const long long idx = (long long)b * G.out_bs + (long long)gr * G.ldo + gc;
+      float4 m4 = *reinterpret_cast<const float4*>(G.st_m + idx);
+      float4 v4 = *reinterpret_cast<const float4*>(G.st_v + idx);
+      const float gg[4] = {g4.x, g4.y, g4.z, g4.w};
+      float mm[4] = {m4.x, m4.y, m4.z, m4.w}, vv[4] = {v4.x, v4.y, v4.z, v4.w}, uu[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        mm[e] = fmaf(G.b1, mm[e], (1.f - G.b1) * gg[e]);
+        vv[e] = fmaf(G.b2, vv[e], (1.f - G.b2) * gg[e] * gg[e]);
+        uu[e] = (mm[e] * G.c1) / (sqrtf(vv[e] * G.c2) + G.eps);
+      }
+      *reinterpret_cast<float4*>(G.st_m + idx) = make_float4(mm[0], mm[1], mm[2], mm[3]);
+      *reinterpret_cast<float4*>(G.st_v + idx) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      uint2 u2;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u2);
+      h[0] = __floats2bfloat162_rn(uu[0], uu[1]);
+      h[1] = __floats2bfloat162_rn(uu[2], uu[3]);
+      *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(G.out) + idx) = u2;
+    }
+    return;
+  }
   // buffers of chunk k-2 must have been read by their TMA store
   if (lane == 0) bulk_wait_read<1>();
   __syncwarp();

@@ -107,8 +107,12 @@ inline void setup_out_map(GemmParams& p, int g) {
   using T = EpiT<EPI>;
   GroupDesc& G = p.g[g];
   G.tma_out = 0;
-  if (EPI == EPI_SOAP_ADAM) return;  // reads and writes four arrays: direct-store epilogue
   auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  if (EPI == EPI_SOAP_ADAM) {  // coalesced staged path without TMA: 16-byte m / v, 8-byte u vectors
+    G.tma_out = (G.N % 4 == 0) && (G.ldo % 4 == 0) && (G.out_bs % 4 == 0) && a16(G.st_m) && a16(G.st_v) &&
+                ((reinterpret_cast<uintptr_t>(G.out) & 7) == 0);
+    return;
+  }
   if (!G.out || !a16(G.out) || (G.ldo * T::ESZ) % 16 || (G.out_bs * T::ESZ) % 16 || G.N % T::EPV) return;
   if (T::AUX && (!G.aux || !a16(G.aux) || (G.ld_aux * T::ESZ) % 16 || (G.aux_bs * T::ESZ) % 16)) return;
   const int rows = G.out_trans ? G.N : G.M;

@@ -13,9 +13,9 @@
 // two-sided product and coupled_newton_one (shampoo.py:277-347) for the roots.
 //
 // Operands are bf16 with fp32 accumulation. Each two-sided product is two
-// chained GEMMs, the cheaper association first; the intermediate is kept as a
-// bf16 hi + lo pair, so only operand rounding (not intermediate rounding)
-// separates the result from an fp32 evaluation.
+// chained GEMMs, the cheaper association first. Shampoo keeps its intermediate
+// as a bf16 hi + lo pair (fp32-level apply); the SOAP chain rounds its
+// intermediates and the Adam direction to bf16 like every other operand.
 #include "runtime.cuh"
 
 namespace lsr {
@@ -99,7 +99,7 @@ extern "C" {
 
 size_t lsr_soap_workspace_bytes(int batch, int rows, int cols) {
   if (!dims_ok(batch, rows, cols)) return 0;
-  return 4 * a256((size_t)std::max(batch, 1) * rows * cols * 2) + 256;  // two bf16 hi/lo pairs
+  return 2 * a256((size_t)std::max(batch, 1) * rows * cols * 2) + 256;  // bf16 intermediate + direction
 }
 
 int lsr_soap_direction_bf16(const void* G, float* L, float* R, const void* QL, const void* QR, float* m, float* v,
@@ -113,22 +113,21 @@ int lsr_soap_direction_bf16(const void* G, float* L, float* R, const void* QL, c
   if (!ws || ws_bytes < lsr_soap_workspace_bytes(batch, rows, cols)) return LSR_ERR_WORKSPACE;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int r = rows, c = cols, B = batch;
-  const size_t rc2 = a256((size_t)B * r * c * 2);
   uint8_t* w = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(ws), 256));
-  void* P1h = w;            // first intermediate pair, later the back-rotation intermediate
-  void* P1l = w + rc2;
-  void* Uh = w + 2 * rc2;   // rotated Adam direction (hi/lo)
-  void* Ul = w + 3 * rc2;
+  void* P1 = w;                                   // bf16 intermediate of each two-sided product
+  void* Ud = w + a256((size_t)B * r * c * 2);     // bf16 Adam direction in the rotated basis
   if (update_stats) {
     rc = stats_update(G, L, R, B, r, c, beta2, stream);
     if (rc) return rc;
   }
+  // Every GEMM operand is bf16 (the intermediates included), accumulation fp32;
+  // each two-sided product runs the cheaper association first.
   const bool right_first = c > r;
   // ---- G' = Q_L^T G Q_R, Adam fused into the second GEMM's epilogue
   {
     GemmParams p{};
     p.ngroups = 1;
-    out_desc(p.g[0], B, r, c, P1h, P1l);
+    out_desc(p.g[0], B, r, c, P1, nullptr);
     if (right_first) {  // S = G Q_R : (i,k) = G[i][k], (j,k) = Q_R[k][j]
       const Operand pr[1][2] = {{bmat(G, r, c, B, 0), bmat(QR, c, c, B, 1)}};
       rc = set_pairs(p, pr, 1, cdiv(c, BK));
@@ -136,14 +135,14 @@ int lsr_soap_direction_bf16(const void* G, float* L, float* R, const void* QL, c
       const Operand pr[1][2] = {{bmat(QL, r, r, B, 1), bmat(G, r, c, B, 1)}};
       rc = set_pairs(p, pr, 1, cdiv(r, BK));
     }
-    if (!rc) rc = launch_gemm<S_BN, EPI_SPLIT_BF16X2>(p, st);
+    if (!rc) rc = launch_gemm<S_BN, EPI_STORE_BF16>(p, st);
     if (rc) return rc;
   }
   {
     GemmParams p{};
     p.ngroups = 1;
     GroupDesc& Gd = p.g[0];
-    out_desc(Gd, B, r, c, Uh, Ul);
+    out_desc(Gd, B, r, c, Ud, nullptr);
     Gd.st_m = m;
     Gd.st_v = v;
     Gd.b1 = beta1;
@@ -152,13 +151,11 @@ int lsr_soap_direction_bf16(const void* G, float* L, float* R, const void* QL, c
     Gd.c2 = (float)(1.0 / (1.0 - std::pow((double)beta2, step)));
     Gd.eps = eps;
     if (right_first) {  // G' = Q_L^T S : (i,k) = Q_L[k][i], (j,k) = S[k][j]
-      const Operand pr[2][2] = {{bmat(QL, r, r, B, 1), bmat(P1h, r, c, B, 1)},
-                                {bmat(QL, r, r, B, 1), bmat(P1l, r, c, B, 1)}};
-      rc = set_pairs(p, pr, 2, cdiv(r, BK));
+      const Operand pr[1][2] = {{bmat(QL, r, r, B, 1), bmat(P1, r, c, B, 1)}};
+      rc = set_pairs(p, pr, 1, cdiv(r, BK));
     } else {  // G' = T Q_R : (i,k) = T[i][k], (j,k) = Q_R[k][j]
-      const Operand pr[2][2] = {{bmat(P1h, r, c, B, 0), bmat(QR, c, c, B, 1)},
-                                {bmat(P1l, r, c, B, 0), bmat(QR, c, c, B, 1)}};
-      rc = set_pairs(p, pr, 2, cdiv(c, BK));
+      const Operand pr[1][2] = {{bmat(P1, r, c, B, 0), bmat(QR, c, c, B, 1)}};
+      rc = set_pairs(p, pr, 1, cdiv(c, BK));
     }
     if (!rc) rc = launch_gemm<S_BN, EPI_SOAP_ADAM>(p, st);
     if (rc) return rc;
@@ -167,30 +164,26 @@ int lsr_soap_direction_bf16(const void* G, float* L, float* R, const void* QL, c
   {
     GemmParams p{};
     p.ngroups = 1;
-    out_desc(p.g[0], B, r, c, P1h, P1l);
+    out_desc(p.g[0], B, r, c, P1, nullptr);
     if (right_first) {  // V = U' Q_R^T : (i,k) = U'[i][k], (j,k) = Q_R[j][k]
-      const Operand pr[2][2] = {{bmat(Uh, r, c, B, 0), bmat(QR, c, c, B, 0)},
-                                {bmat(Ul, r, c, B, 0), bmat(QR, c, c, B, 0)}};
-      rc = set_pairs(p, pr, 2, cdiv(c, BK));
+      const Operand pr[1][2] = {{bmat(Ud, r, c, B, 0), bmat(QR, c, c, B, 0)}};
+      rc = set_pairs(p, pr, 1, cdiv(c, BK));
     } else {  // T = Q_L U' : (i,k) = Q_L[i][k], (j,k) = U'[k][j]
-      const Operand pr[2][2] = {{bmat(QL, r, r, B, 0), bmat(Uh, r, c, B, 1)},
-                                {bmat(QL, r, r, B, 0), bmat(Ul, r, c, B, 1)}};
-      rc = set_pairs(p, pr, 2, cdiv(r, BK));
+      const Operand pr[1][2] = {{bmat(QL, r, r, B, 0), bmat(Ud, r, c, B, 1)}};
+      rc = set_pairs(p, pr, 1, cdiv(r, BK));
     }
-    if (!rc) rc = launch_gemm<S_BN, EPI_SPLIT_BF16X2>(p, st);
+    if (!rc) rc = launch_gemm<S_BN, EPI_STORE_BF16>(p, st);
     if (rc) return rc;
   }
   GemmParams p{};
   p.ngroups = 1;
   out_desc(p.g[0], B, r, c, U, nullptr);
   if (right_first) {  // U = Q_L V : (i,k) = Q_L[i][k], (j,k) = V[k][j]
-    const Operand pr[2][2] = {{bmat(QL, r, r, B, 0), bmat(P1h, r, c, B, 1)},
-                              {bmat(QL, r, r, B, 0), bmat(P1l, r, c, B, 1)}};
-    rc = set_pairs(p, pr, 2, cdiv(r, BK));
+    const Operand pr[1][2] = {{bmat(QL, r, r, B, 0), bmat(P1, r, c, B, 1)}};
+    rc = set_pairs(p, pr, 1, cdiv(r, BK));
   } else {  // U = T Q_R^T : (i,k) = T[i][k], (j,k) = Q_R[j][k]
-    const Operand pr[2][2] = {{bmat(P1h, r, c, B, 0), bmat(QR, c, c, B, 0)},
-                              {bmat(P1l, r, c, B, 0), bmat(QR, c, c, B, 0)}};
-    rc = set_pairs(p, pr, 2, cdiv(c, BK));
+    const Operand pr[1][2] = {{bmat(P1, r, c, B, 0), bmat(QR, c, c, B, 0)}};
+    rc = set_pairs(p, pr, 1, cdiv(c, BK));
   }
   return rc ? rc : launch_gemm<S_BN, EPI_STORE_F32>(p, st);
 }

@@ -241,7 +241,9 @@ LSR_API int lsr_kron_reconstruct_f32(const float* const* factors, const int* row
  *   then G' = Q_L^T G Q_R and Adam in that basis (fused into the rotation):
  *     m = beta1 m + (1-beta1) G',  v = beta2 v + (1-beta2) G'^2,
  *     U' = (m / (1-beta1^step)) / (sqrt(v / (1-beta2^step)) + eps),
- *   and the update direction U = Q_L U' Q_R^T (fp32).
+ *   and the update direction U = Q_L U' Q_R^T (fp32). Every GEMM operand of
+ *   the chain is bf16: the intermediates (G Q_R or Q_L^T G, then U' Q_R^T or
+ *   Q_L U', the cheaper association first) and U' are rounded to bf16.
  *   L fp32 [b][r][r], R fp32 [b][c][c], Q_L bf16 [b][r][r], Q_R bf16 [b][c][c],
  *   m, v fp32 [b][r][c]; rows, cols multiples of 8.
  * lsr_shampoo_direction_bf16: optional statistics update as above, then

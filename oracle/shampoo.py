@@ -44,15 +44,27 @@ def shampoo_precondition(G, Lroot, Rroot):
     return np.asarray(Lroot, np.float64) @ np.asarray(G, np.float64) @ np.asarray(Rroot, np.float64)
 
 
-def soap_direction(G, QL, QR, m, v, beta1, beta2, eps, step):
-    """Returns (U, m, v) for one SOAP step in the eigenbases QL, QR."""
+def soap_direction(G, QL, QR, m, v, beta1, beta2, eps, step, bf16_operands=False):
+    """Returns (U, m, v) for one SOAP step in the eigenbases QL, QR.
+
+    bf16_operands=True rounds every GEMM operand to bf16 as the kernels do: the
+    intermediate of each two-sided product (cheaper association first: G Q_R
+    then Q_L^T (.) when cols > rows, else Q_L^T G then (.) Q_R) and the Adam
+    direction U'.
+    """
+    from .bf16 import round_bf16
+    rd = (lambda x: round_bf16(np.asarray(x, np.float32)).astype(np.float64)) if bf16_operands else (lambda x: x)
     QL = np.asarray(QL, np.float64)
     QR = np.asarray(QR, np.float64)
-    Gr = np.swapaxes(QL, -1, -2) @ np.asarray(G, np.float64) @ QR
+    QLt = np.swapaxes(QL, -1, -2)
+    G = np.asarray(G, np.float64)
+    right_first = G.shape[-1] > G.shape[-2]
+    Gr = QLt @ rd(G @ QR) if right_first else rd(QLt @ G) @ QR
     m = beta1 * np.asarray(m, np.float64) + (1.0 - beta1) * Gr
     v = beta2 * np.asarray(v, np.float64) + (1.0 - beta2) * Gr * Gr
-    Up = (m / (1.0 - beta1 ** step)) / (np.sqrt(v / (1.0 - beta2 ** step)) + eps)
-    U = QL @ Up @ np.swapaxes(QR, -1, -2)
+    Up = rd((m / (1.0 - beta1 ** step)) / (np.sqrt(v / (1.0 - beta2 ** step)) + eps))
+    QRt = np.swapaxes(QR, -1, -2)
+    U = QL @ rd(Up @ QRt) if right_first else rd(QL @ Up) @ QRt
     return U, m, v
 
 

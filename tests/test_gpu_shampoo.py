@@ -37,7 +37,7 @@ def test_soap_direction(shape):
     Gn = G.float().numpy()
     Lr, Rr = osh.stats_update(L0.numpy(), R0.numpy(), Gn, 0.95)
     Ur, mr, vr = osh.soap_direction(Gn, QL.float().numpy(), QR.float().numpy(), m0.numpy(), v0.numpy(),
-                                    0.95, 0.95, 1e-8, 5)
+                                    0.95, 0.95, 1e-8, 5, bf16_operands=True)
     assert rel_fro(L.cpu().numpy(), Lr) < 1e-5
     assert rel_fro(R.cpu().numpy(), Rr) < 1e-5
     assert rel_fro(m.cpu().numpy(), mr) < TOL
@@ -86,7 +86,8 @@ def test_distributed_shampoo_soap_plumbing():
             r, c = shape
             Gb = grads[i].float().numpy()[r0:r0 + r, c0:c0 + c]
             U, _, _ = osh.soap_direction(Gb, grp.QL[k].float().cpu().numpy(), grp.QR[k].float().cpu().numpy(),
-                                         np.zeros((r, c)), np.zeros((r, c)), 0.95, 0.95, 1e-8, 1)
+                                         np.zeros((r, c)), np.zeros((r, c)), 0.95, 0.95, 1e-8, 1,
+                                         bf16_operands=True)
             p_ref = P0[i].float().numpy()[r0:r0 + r, c0:c0 + c] * np.float32(1 - 0.01 * 0.01) - 0.01 * U
             got = params[i].detach().float().cpu().numpy()[r0:r0 + r, c0:c0 + c]
             # parameters are bf16: compare the change
