@@ -523,6 +523,42 @@ def run_workload(args) -> None:
                                       f"{sum(len(grp.refs) for _, grp, _ in opt._groups)} blocks at 1024, 1 GPU",
                           "value": ms, "unit": "ms", "algorithmic_tflop": fl / 1e12, "tflops": fl / ms / 1e9,
                           "frac_of_sustained": fl / ms / 1e9 / peaks["bf16_tflops_sustained"]})
+    elif w == "muon_torch":
+        # The reference's Muon op sequence (muon_lm_ddp.py:554-593, :373-426: momentum,
+        # torch.bmm Newton-Schulz per shape group in chunks of 8, apply) on this GPU
+        # (cuBLAS), on the same 192-matrix workload: the library baseline on B200.
+        shapes, P, G, M = make_params(dev, args.layers)
+        del shapes
+        a_, b_, c_ = 3.4445, -4.7750, 2.0315
+
+        def ref_step():
+            groups = {}
+            for i, p in enumerate(P):
+                groups.setdefault((min(p.shape), max(p.shape)), []).append(i)
+            for _, idx in groups.items():
+                for s0 in range(0, len(idx), 8):
+                    chunk = idx[s0:s0 + 8]
+                    us = []
+                    for i in chunk:
+                        M[i].mul_(MU).add_(G[i])
+                        u = G[i] + MU * M[i]
+                        us.append(u.T if u.shape[0] > u.shape[1] else u)
+                    X = torch.stack(us).bfloat16()
+                    X = X / X.flatten(1).norm(dim=1).clamp(min=EPS)[:, None, None]
+                    for _ in range(NS_STEPS):
+                        A = torch.bmm(X, X.transpose(-1, -2))
+                        B = b_ * A + c_ * torch.bmm(A, A)
+                        X = a_ * X + torch.bmm(B, X)
+                    for k, i in enumerate(chunk):
+                        upd = X[k].T if P[i].shape[0] > P[i].shape[1] else X[k]
+                        P[i].mul_(1 - LR * WD)
+                        ratio = max(1.0, P[i].shape[0] / P[i].shape[1]) ** 0.5
+                        P[i].add_(upd, alpha=-LR * ratio)
+        ms = _time_gpu(ref_step, args.warmup, args.steps)
+        fl = sum(ns_dense_flops(p.shape) for p in P)
+        lines.append({"workload": "reference torch op sequence (cuBLAS bmm, chunks of 8) on the GPT-2-XL Muon step",
+                      "value": ms, "unit": "ms", "dense_tflop": fl / 1e12, "tflops": fl / ms / 1e9,
+                      "frac_of_sustained": fl / ms / 1e9 / peaks["bf16_tflops_sustained"]})
     for ln in lines:
         ln.update({"steps": args.steps, "warmup": args.warmup, "l2": "flushed (256 MB write) before each run",
                    "peak_kind": peaks["source"], "cores": os.cpu_count() or 1})
@@ -538,7 +574,7 @@ def main(argv=None) -> int:
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="GPT-2-XL layers (48 = the full model)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["muon", "cfg1", "cfg2", "cfg3", "cfg5"], default="muon",
+    ap.add_argument("--workload", choices=["muon", "cfg1", "cfg2", "cfg3", "cfg5", "muon_torch"], default="muon",
                     help="muon = the headline GPT-2-XL Muon step (default); cfgN = per-row workloads")
     args = ap.parse_args(argv)
     if args.workload != "muon" and args.impl == "lsr":

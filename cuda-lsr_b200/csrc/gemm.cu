@@ -23,8 +23,10 @@ int lsr_gemm_bf16(const void* A, const void* B, void* D, int batch, int M, int N
   p.ngroups = 1;
   Operand oa = a_trans ? Operand{A, K, M, M, (long long)K * M, batch, 1} : Operand{A, M, K, K, (long long)M * K, batch, 0};
   Operand ob = b_trans ? Operand{B, N, K, K, (long long)N * K, batch, 0} : Operand{B, K, N, N, (long long)K * N, batch, 1};
+  // Problems taller than one 128-row tile run on CTA pairs (256-row tiles, half of B per CTA).
+  const bool pair = M > BM;
   rc = make_operand_map(&p.mapA[0][0], oa, false, G_BN);
-  if (!rc) rc = make_operand_map(&p.mapB[0][0], ob, true, G_BN);
+  if (!rc) rc = make_operand_map(&p.mapB[0][0], ob, true, pair ? G_BN / 2 : G_BN);
   if (rc) return rc;
   GroupDesc& G = p.g[0];
   G.batch = batch;
@@ -37,6 +39,9 @@ int lsr_gemm_bf16(const void* A, const void* B, void* D, int batch, int M, int N
   G.ldo = N;
   G.alpha = alpha;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (pair)
+    return out_f32 ? launch_gemm<G_BN, EPI_STORE_F32, default_stages<EPI_STORE_F32, 1>(), 0, 0, 1>(p, st)
+                   : launch_gemm<G_BN, EPI_STORE_BF16, default_stages<EPI_STORE_BF16, 1>(), 0, 0, 1>(p, st);
   return out_f32 ? launch_gemm<G_BN, EPI_STORE_F32>(p, st) : launch_gemm<G_BN, EPI_STORE_BF16>(p, st);
 }
 
@@ -53,8 +58,9 @@ int lsr_gram_update_f32(const void* Gm, void* S, int batch, int rows, int cols, 
   // side 0: G G^T (operands are rows of G, K-major); side 1: G^T G (columns of G, MN-major)
   Operand o = side == 0 ? Operand{Gm, rows, cols, cols, (long long)rows * cols, batch, 0}
                         : Operand{Gm, rows, cols, cols, (long long)rows * cols, batch, 1};
+  const bool pair = n > BM;
   rc = make_operand_map(&p.mapA[0][0], o, false, G_BN);
-  if (!rc) rc = make_operand_map(&p.mapB[0][0], o, true, G_BN);
+  if (!rc) rc = make_operand_map(&p.mapB[0][0], o, true, pair ? G_BN / 2 : G_BN);
   if (rc) return rc;
   GroupDesc& G = p.g[0];
   G.batch = batch;
@@ -70,6 +76,9 @@ int lsr_gram_update_f32(const void* Gm, void* S, int batch, int rows, int cols, 
   G.ld_aux = n;
   G.alpha = alpha;
   G.beta = beta;
+  if (pair)
+    return launch_gemm<G_BN, EPI_F32_EMA, default_stages<EPI_F32_EMA, 1>(), 0, 0, 1>(
+        p, reinterpret_cast<cudaStream_t>(stream));
   return launch_gemm<G_BN, EPI_F32_EMA>(p, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -103,13 +103,14 @@ struct GemmParams {
   int* status;
 };
 
-template <int BN>
+// First column tile of tile row ti touching the upper triangle (tiles of TM x BN).
+template <int BN, int TM = BM>
 __host__ __device__ constexpr int tri_first_col_tile(int ti) {
-  return (ti * BM) / BN;
+  return (ti * TM) / BN;
 }
 
 // Map a flat tile index to (group, batch entry, tile row, tile column).
-template <int BN>
+template <int BN, int TM = BM>
 __device__ __forceinline__ void decode_tile(const GemmParams& p, int t, int& g, int& b, int& ti, int& tj) {
   g = 0;
 #pragma unroll 1
@@ -126,9 +127,9 @@ __device__ __forceinline__ void decode_tile(const GemmParams& p, int t, int& g, 
     tj = 0;
 #pragma unroll 1
     for (; ti < G.tiles_m; ++ti) {
-      const int cnt = max(0, G.tiles_n - tri_first_col_tile<BN>(ti));
+      const int cnt = max(0, G.tiles_n - tri_first_col_tile<BN, TM>(ti));
       if (r < cnt) {
-        tj = tri_first_col_tile<BN>(ti) + r;
+        tj = tri_first_col_tile<BN, TM>(ti) + r;
         break;
       }
       r -= cnt;
@@ -549,10 +550,12 @@ __device__ __forceinline__ void epilogue_chunk_staged(const GemmParams& p, int g
 // The kernel
 // ---------------------------------------------------------------------------
 
-template <int BN, int STAGES, int EPI>
+// PAIR = 1: the tile is computed by a cluster of two CTAs; each CTA holds
+// 128 rows of A and BN/2 rows of B per stage.
+template <int BN, int STAGES, int EPI, int PAIR = 0>
 struct GemmSmem {
   static constexpr int A_BYTES = BM * 128;  // 128-byte K rows, for bf16 and tf32 alike
-  static constexpr int B_BYTES = BN * 128;
+  static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;
   static constexpr int EPI_BYTES = (kEpiThreads / 32) * 4 * EpiT<EPI>::CHB;  // per warp: 2 direct + 2 transposed
@@ -562,9 +565,9 @@ struct GemmSmem {
 };
 
 // Pipeline depth that fits next to the epilogue staging buffers.
-template <int EPI>
+template <int EPI, int PAIR = 0>
 constexpr int default_stages() {
-  return EpiT<EPI>::F32 ? 3 : 4;
+  return PAIR ? (EpiT<EPI>::F32 ? 5 : 6) : (EpiT<EPI>::F32 ? 3 : 4);
 }
 
 // TF32 = 0: bf16 operands (kind::f16); TF32 = 1: fp32 operands read as tf32
@@ -574,15 +577,25 @@ constexpr int default_stages() {
 // the epilogue adds in fp32; the tensor core's accumulation then never adds
 // small correction products into a large running sum (3xTF32 accuracy). One
 // tile's accumulators fill TMEM, so tiles are not double-buffered.
-template <int BN, int STAGES, int EPI, int TF32, int DUAL>
+// PAIR = 1: launched as clusters of two CTAs. A tile is 256 x BN; CTA rank r
+// loads rows [128 r, 128 r + 128) of A and rows [r BN/2, (r+1) BN/2) of B, the
+// leader (rank 0) issues tcgen05.mma.cta_group::2 (M = 256) reading both CTAs'
+// shared memory, and each CTA's TMEM holds its 128 output rows. The peer's TMA
+// loads count on the leader's full barriers; the leader's commits arrive on
+// both CTAs' barriers; both epilogues arrive on the leader's accumulator-empty
+// barriers. No multicast is used.
+template <int BN, int STAGES, int EPI, int TF32, int DUAL, int PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __grid_constant__ GemmParams p) {
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 64 in [64, 256]");
   constexpr int KE = TF32 ? BK_TF32 : BK;        // elements per K block (= MN elements per MN-major chunk)
   constexpr int CHUNK = KE * 128;                // bytes of one MN-major chunk (KE K-rows of 128 B)
   constexpr uint32_t MN_STEP = (TF32 ? 8 : 16) * 128;  // bytes between UMMA K steps, MN-major
   constexpr int ACC_COLS = DUAL ? 2 * BN : BN;          // TMEM columns per tile in flight
+  constexpr int TM = PAIR ? 2 * BM : BM;                // output rows per tile
+  constexpr int BNC = PAIR ? BN / 2 : BN;               // B rows loaded by this CTA
   static_assert(2 * BN <= 512, "two BN-wide accumulators must fit in TMEM");
-  using L = GemmSmem<BN, STAGES, EPI>;
+  static_assert(!PAIR || BNC % KE == 0, "pair B half must be whole MN-major chunks");
+  using L = GemmSmem<BN, STAGES, EPI, PAIR>;
   using ET = EpiT<EPI>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -598,6 +611,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int tile_first = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tile_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -606,7 +622,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull + a, 1);
-      mbar_init(tempty + a, kEpiThreads);
+      mbar_init(tempty + a, kEpiThreads * (PAIR ? 2 : 1));
     }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
@@ -620,11 +636,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
       }
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();  // both CTAs' barriers initialised before any cross-CTA use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -634,11 +656,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+      for (int t = tile_first; ok && t < p.total_tiles; t += tile_step) {
         int g, b, ti, tj;
-        decode_tile<BN>(p, t, g, b, ti, tj);
+        decode_tile<BN, TM>(p, t, g, b, ti, tj);
         const GroupDesc& G = p.g[g];
-        const int m0 = ti * BM, n0 = tj * BN;
+        const int m0 = ti * TM + (int)rank * BM, n0 = tj * BN + (int)rank * BNC;
         for (int sg = 0; ok && sg < G.nseg; ++sg) {
           const SegDesc S = G.seg[sg];
           const CUtensorMap* ma = &p.mapA[g][sg];
@@ -652,19 +674,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
             }
             uint8_t* sa = smem + s * L::STAGE_BYTES;
             uint8_t* sb = sa + L::A_BYTES;
-            mbar_arrive_expect_tx(full + s, L::STAGE_BYTES);
             const int k0 = kb * KE;
-            if (!S.a_mn) {
-              tma_load_3d(sa, ma, full + s, k0, m0, za);
-            } else {
+            if constexpr (PAIR) {
+              // the leader's full barrier counts both CTAs' bytes
+              if (rank == 0) mbar_arrive_expect_tx(full + s, 2 * L::STAGE_BYTES);
+              const uint32_t fb = mapa_shared(smem_u32(full + s), 0);
+              if (!S.a_mn) {
+                tma_load_3d_pair(sa, ma, fb, k0, m0, za);
+              } else {
 #pragma unroll
-              for (int c = 0; c < BM / KE; ++c) tma_load_3d(sa + c * CHUNK, ma, full + s, m0 + KE * c, k0, za);
-            }
-            if (!S.b_mn) {
-              tma_load_3d(sb, mb, full + s, k0, n0, zb);
-            } else {
+                for (int c = 0; c < BM / KE; ++c) tma_load_3d_pair(sa + c * CHUNK, ma, fb, m0 + KE * c, k0, za);
+              }
+              if (!S.b_mn) {
+                tma_load_3d_pair(sb, mb, fb, k0, n0, zb);
+              } else {
 #pragma unroll
-              for (int c = 0; c < BN / KE; ++c) tma_load_3d(sb + c * CHUNK, mb, full + s, n0 + KE * c, k0, zb);
+                for (int c = 0; c < BNC / KE; ++c) tma_load_3d_pair(sb + c * CHUNK, mb, fb, n0 + KE * c, k0, zb);
+              }
+            } else {
+              mbar_arrive_expect_tx(full + s, L::STAGE_BYTES);
+              if (!S.a_mn) {
+                tma_load_3d(sa, ma, full + s, k0, m0, za);
+              } else {
+#pragma unroll
+                for (int c = 0; c < BM / KE; ++c) tma_load_3d(sa + c * CHUNK, ma, full + s, m0 + KE * c, k0, za);
+              }
+              if (!S.b_mn) {
+                tma_load_3d(sb, mb, full + s, k0, n0, zb);
+              } else {
+#pragma unroll
+                for (int c = 0; c < BN / KE; ++c) tma_load_3d(sb + c * CHUNK, mb, full + s, n0 + KE * c, k0, zb);
+              }
             }
             if (++s == STAGES) {
               s = 0;
@@ -676,16 +716,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (pair: leader only)
+    if (lane == 0 && rank == 0) {
       int s = 0;
       uint32_t ph = 0;
       int acc = 0;
       uint32_t aph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+      for (int t = tile_first; ok && t < p.total_tiles; t += tile_step) {
         int g, b, ti, tj;
-        decode_tile<BN>(p, t, g, b, ti, tj);
+        decode_tile<BN, TM>(p, t, g, b, ti, tj);
         const GroupDesc& G = p.g[g];
         if (!mbar_wait(tempty + acc, aph ^ 1, abort_flag, p.status, ST_TIMEOUT_MMA_TMEM)) break;
         tc_fence_after();
@@ -697,7 +737,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
           const uint32_t d_tmem = d_base + static_cast<uint32_t>(slot * BN);
           uint32_t accumulate = (acc_flags >> slot) & 1u;
           acc_flags |= 1u << slot;
-          const uint32_t idesc = make_idesc(BM, BN, TF32 ? 2u : 1u, (uint32_t)S.a_mn, (uint32_t)S.b_mn);
+          const uint32_t idesc = make_idesc(TM, BN, TF32 ? 2u : 1u, (uint32_t)S.a_mn, (uint32_t)S.b_mn);
           // per-UMMA descriptor advance along K, in 16-byte units: 32 B within a
           // K-major row, MN_STEP bytes (UMMA_K rows) for MN-major
           const uint32_t a_step = S.a_mn ? (MN_STEP >> 4) : (32u >> 4);
@@ -714,13 +754,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
             const uint64_t bdesc = S.b_mn ? smem_desc_sw128(sb, CHUNK, 1024) : smem_desc_sw128(sb, 16, 1024);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-              if constexpr (TF32)
-                umma_tf32(d_tmem, adesc + (uint64_t)(k * a_step), bdesc + (uint64_t)(k * b_step), idesc, accumulate);
-              else
-                umma_bf16(d_tmem, adesc + (uint64_t)(k * a_step), bdesc + (uint64_t)(k * b_step), idesc, accumulate);
+              const uint64_t ad = adesc + (uint64_t)(k * a_step), bd = bdesc + (uint64_t)(k * b_step);
+              if constexpr (PAIR) {
+                if constexpr (TF32)
+                  umma_tf32_pair(d_tmem, ad, bd, idesc, accumulate);
+                else
+                  umma_bf16_pair(d_tmem, ad, bd, idesc, accumulate);
+              } else {
+                if constexpr (TF32)
+                  umma_tf32(d_tmem, ad, bd, idesc, accumulate);
+                else
+                  umma_bf16(d_tmem, ad, bd, idesc, accumulate);
+              }
               accumulate = 1;
             }
-            umma_commit(empty + s);  // frees this smem stage once the MMAs have read it
+            // frees this smem stage (in both CTAs of a pair) once the MMAs have read it
+            if constexpr (PAIR) {
+              umma_commit_pair(mapa_shared(smem_u32(empty + s), 0));
+              umma_commit_pair(mapa_shared(smem_u32(empty + s), 1));
+            } else {
+              umma_commit(empty + s);
+            }
             if (++s == STAGES) {
               s = 0;
               ph ^= 1;
@@ -728,7 +782,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
           }
         }
         if (!ok) break;
-        umma_commit(tfull + acc);  // accumulator ready for the epilogue
+        // accumulator ready for the epilogue(s)
+        if constexpr (PAIR) {
+          umma_commit_pair(mapa_shared(smem_u32(tfull + acc), 0));
+          umma_commit_pair(mapa_shared(smem_u32(tfull + acc), 1));
+        } else {
+          umma_commit(tfull + acc);
+        }
         if (DUAL) {
           aph ^= 1;
         } else {
@@ -737,7 +797,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
         }
       }
       // Drain: make sure no MMA is still writing TMEM before it is released.
-      umma_commit(done_bar);
+      if constexpr (PAIR)
+        umma_commit_pair(mapa_shared(smem_u32(done_bar), 0));
+      else
+        umma_commit(done_bar);
       const uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(done_bar, 0)) {
         if (globaltimer_ns() - t0 > LSR_WAIT_TIMEOUT_NS) {
@@ -754,11 +817,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
     int acc = 0;
     uint32_t aph = 0;
     uint32_t kchunk = 0;  // chunks processed by this warp (staging buffer parity)
-    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+    for (int t = tile_first; t < p.total_tiles; t += tile_step) {
       int g, b, ti, tj;
-      decode_tile<BN>(p, t, g, b, ti, tj);
+      decode_tile<BN, TM>(p, t, g, b, ti, tj);
       const GroupDesc& G = p.g[g];
-      const int row0 = ti * BM + q * 32;  // first row of this warp
+      const int row0 = ti * TM + (int)rank * BM + q * 32;  // first row of this warp
       // warp-uniform mask of live 32-column chunks
       uint32_t live = 0;
       if (row0 < G.M) {
@@ -814,7 +877,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
         }
       }
       tc_fence_before();
-      mbar_arrive(tempty + acc);
+      if constexpr (PAIR)
+        mbar_arrive_cluster(mapa_shared(smem_u32(tempty + acc), 0));  // the leader's MMA waits on it
+      else
+        mbar_arrive(tempty + acc);
       if (DUAL) {
         aph ^= 1;
       } else {
@@ -828,9 +894,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
 
   tc_fence_before();
   __syncthreads();
+  // Pair: neither CTA releases TMEM or exits while the other may still read its
+  // shared memory (leader MMAs) or arrive on its barriers (peer epilogue).
+  if constexpr (PAIR) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 512);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, 512);
+    else
+      tmem_dealloc(tmem_base, 512);
   }
 }
 

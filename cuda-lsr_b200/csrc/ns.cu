@@ -413,8 +413,22 @@ int normalize_group(NsGroup& G, float eps, cudaStream_t st) {
 }
 
 // `steps` quintic iterations over up to kMaxGroups groups.
+template <int EPI>
+int launch_ns(GemmParams& p, cudaStream_t st, int kind, bool pair) {
+  if (pair) return launch_gemm<NS_BN, EPI, default_stages<EPI, 1>(), 0, 0, 1>(p, st, kind);
+  return launch_gemm<NS_BN, EPI>(p, st, kind);
+}
+
 int ns_iterations(NsGroup* gs, int ng, int steps, float a, float b, float c, cudaStream_t st) {
   constexpr int BN = NS_BN;
+  // Matrices taller than one 128-row tile run on CTA pairs: 256-row tiles, each
+  // CTA loading half of operand B, so the tensor cores need a third less
+  // operand bandwidth per flop.
+  bool pair = false;
+#ifndef LSR_NS_SINGLE_CTA
+  for (int g = 0; g < ng; ++g) pair |= gs[g].m > BM;
+#endif
+  const int BB = pair ? BN / 2 : BN;  // operand-B box rows
   for (int it = 0; it < steps; ++it) {
     const int cur = it & 1, nxt = cur ^ 1;
     const bool last = it == steps - 1;
@@ -426,7 +440,7 @@ int ns_iterations(NsGroup* gs, int ng, int steps, float a, float b, float c, cud
       // phase 1: A = X X^T
       Operand xk{S.X[cur], S.m, S.n, S.ldn, xbs, S.batch, 0};
       int rc = make_operand_map(&p1.mapA[g][0], xk, false, BN);
-      if (!rc) rc = make_operand_map(&p1.mapB[g][0], xk, true, BN);
+      if (!rc) rc = make_operand_map(&p1.mapB[g][0], xk, true, BB);
       GroupDesc& G1 = p1.g[g];
       G1.batch = S.batch;
       G1.M = G1.N = S.m;
@@ -440,7 +454,7 @@ int ns_iterations(NsGroup* gs, int ng, int steps, float a, float b, float c, cud
       // phase 2: B = b A + c A A
       Operand ak{S.A, S.m, S.m, S.ldm, abs_, S.batch, 0};
       if (!rc) rc = make_operand_map(&p2.mapA[g][0], ak, false, BN);
-      if (!rc) rc = make_operand_map(&p2.mapB[g][0], ak, true, BN);
+      if (!rc) rc = make_operand_map(&p2.mapB[g][0], ak, true, BB);
       GroupDesc& G2 = p2.g[g];
       G2.batch = S.batch;
       G2.M = G2.N = S.m;
@@ -459,7 +473,7 @@ int ns_iterations(NsGroup* gs, int ng, int steps, float a, float b, float c, cud
       Operand bk{S.B, S.m, S.m, S.ldm, abs_, S.batch, 0};
       Operand xmn{S.X[cur], S.m, S.n, S.ldn, xbs, S.batch, 1};
       if (!rc) rc = make_operand_map(&p3.mapA[g][0], bk, false, BN);
-      if (!rc) rc = make_operand_map(&p3.mapB[g][0], xmn, true, BN);
+      if (!rc) rc = make_operand_map(&p3.mapB[g][0], xmn, true, BB);
       if (rc) return rc;
       GroupDesc& G3 = p3.g[g];
       G3.batch = S.batch;
@@ -483,9 +497,9 @@ int ns_iterations(NsGroup* gs, int ng, int steps, float a, float b, float c, cud
         G3.ldo = S.ldn;
       }
     }
-    int rc = launch_gemm<BN, EPI_NS_GRAM>(p1, st, PK_GEMM_GRAM);
-    if (!rc) rc = launch_gemm<BN, EPI_NS_POLY>(p2, st, PK_GEMM_POLY);
-    if (!rc) rc = launch_gemm<BN, EPI_NS_UPDATE>(p3, st, PK_GEMM_UPDATE);
+    int rc = launch_ns<EPI_NS_GRAM>(p1, st, PK_GEMM_GRAM, pair);
+    if (!rc) rc = launch_ns<EPI_NS_POLY>(p2, st, PK_GEMM_POLY, pair);
+    if (!rc) rc = launch_ns<EPI_NS_UPDATE>(p3, st, PK_GEMM_UPDATE, pair);
     if (rc) return rc;
   }
   return LSR_OK;

@@ -78,19 +78,19 @@ inline int make_operand_map(CUtensorMap* map, const Operand& o, bool is_b, int B
                         (uint64_t)o.ld, (uint64_t)std::max<long long>(o.bs, (long long)o.rows * o.ld), ke, box_outer);
 }
 
-// Fill tile counts and the flat tile numbering of every group.
-template <int BN>
+// Fill tile counts and the flat tile numbering of every group (tiles of TM x BN).
+template <int BN, int TM = BM>
 inline void finalize_tiles(GemmParams& p) {
   int t = 0;
   for (int g = 0; g < p.ngroups; ++g) {
     GroupDesc& G = p.g[g];
-    G.tiles_m = cdiv(G.M, BM);
+    G.tiles_m = cdiv(G.M, TM);
     G.tiles_n = cdiv(G.N, BN);
     if (!G.tri) {
       G.tiles_per_mat = G.tiles_m * G.tiles_n;
     } else {
       int c = 0;
-      for (int ti = 0; ti < G.tiles_m; ++ti) c += std::max(0, G.tiles_n - tri_first_col_tile<BN>(ti));
+      for (int ti = 0; ti < G.tiles_m; ++ti) c += std::max(0, G.tiles_n - tri_first_col_tile<BN, TM>(ti));
       G.tiles_per_mat = c;
     }
     G.tile_begin = t;
@@ -134,21 +134,41 @@ inline void setup_out_map(GemmParams& p, int g) {
   G.tma_out = 1;
 }
 
-template <int BN, int EPI, int STAGES = default_stages<EPI>(), int TF32 = 0, int DUAL = 0>
+// Launch the engine. PAIR = 1 launches clusters of two CTAs (256-row tiles;
+// the caller builds operand-B tensor maps with BN / 2-row boxes).
+template <int BN, int EPI, int STAGES = default_stages<EPI>(), int TF32 = 0, int DUAL = 0, int PAIR = 0>
 inline int launch_gemm(GemmParams& p, cudaStream_t st, int kind = PK_GEMM_OTHER) {
-  using L = GemmSmem<BN, STAGES, EPI>;
+  using L = GemmSmem<BN, STAGES, EPI, PAIR>;
   static_assert(L::TOTAL <= 232448, "shared memory budget exceeded");
-  finalize_tiles<BN>(p);
+  constexpr int TM = PAIR ? 2 * BM : BM;
+  finalize_tiles<BN, TM>(p);
   if (p.total_tiles == 0) return LSR_OK;
   for (int g = 0; g < p.ngroups; ++g) setup_out_map<EPI>(p, g);
   p.status = status_ptr();
   if (!p.status) return LSR_ERR_LAUNCH;
-  auto kfn = gemm_sm100_kernel<BN, STAGES, EPI, TF32, DUAL>;
+  auto kfn = gemm_sm100_kernel<BN, STAGES, EPI, TF32, DUAL, PAIR>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL) != cudaSuccess)
     return LSR_ERR_LAUNCH;
-  const int grid = std::min(device_sm_count(), p.total_tiles);
   ProfScope prof(kind, st);
-  kfn<<<grid, kGemmThreads, L::TOTAL, st>>>(p);
+  if constexpr (PAIR) {
+    const int clusters = std::min(device_sm_count() / 2, p.total_tiles);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * clusters);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = L::TOTAL;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kfn, p) != cudaSuccess) return LSR_ERR_LAUNCH;
+  } else {
+    const int grid = std::min(device_sm_count(), p.total_tiles);
+    kfn<<<grid, kGemmThreads, L::TOTAL, st>>>(p);
+  }
   return cudaGetLastError() == cudaSuccess ? LSR_OK : LSR_ERR_LAUNCH;
 }
 
