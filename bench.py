@@ -246,7 +246,7 @@ def run_lsr(args) -> None:
         step = opt.muon_step
     else:
         opt = ShardedMuon(params, lr=LR, momentum=MU, nesterov=True, weight_decay=WD, ns_steps=NS_STEPS, eps=EPS,
-                          flat_params=True)
+                          flat_params=True, exchange=args.exchange)
         for Gp in opt.groups:
             for k, j in enumerate(Gp.owned):
                 idx = next(i for i, p in enumerate(params) if p is Gp.params[j])
@@ -334,7 +334,8 @@ def run_lsr(args) -> None:
             "vs_baseline": round(ms / BASELINE_MS, 4), "dtype": "bf16",
             "data": "synthetic (seeded N(0,0.01^2) grads/momentum, N(0,0.02^2) params, generated on device)",
             "config": {"workload": WORKLOAD, "layers": args.layers, "ns_steps": NS_STEPS,
-                       "parallelism": "single gpu" if world == 1 else f"zero1 round-robin shards x{world}",
+                       "parallelism": "single gpu" if world == 1 else
+                       f"zero1 round-robin shards x{world}, {args.exchange} exchange",
                        "l2": "inputs larger than L2 (8.8 GB params+grads+momentum)"},
             "roofline": roofline, "clocks": clocks, "gpu_launches": int(launches), "e2e": e2e,
             "cpu_baseline": cpu,
@@ -342,6 +343,7 @@ def run_lsr(args) -> None:
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
+        opt.close()
         dist.barrier()
         dist.destroy_process_group()
 
@@ -573,6 +575,8 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=["lsr", "reference"], default="lsr")
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="GPT-2-XL layers (48 = the full model)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="N>1: parameter exchange (peer-memory push or NCCL all-gather)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["muon", "cfg1", "cfg2", "cfg3", "cfg5", "muon_torch"], default="muon",
                     help="muon = the headline GPT-2-XL Muon step (default); cfgN = per-row workloads")

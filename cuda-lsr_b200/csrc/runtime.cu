@@ -152,6 +152,7 @@ const char* lsr_strerror(int code) {
     case LSR_ERR_DRIVER: return "TMA tensor map encoding failed";
     case LSR_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
     case LSR_ERR_TOO_LARGE: return "problem exceeds the fixed scratch capacity of the allocation-free entry point";
+    case LSR_ERR_PEER: return "CUDA IPC / peer memory call failed";
     default: return "unknown liblsr error";
   }
 }

@@ -34,7 +34,8 @@ enum ProfKind : int {
   PK_EW_APPLY = 5,      // parameter update
   PK_GEMM_OTHER = 6,    // plain GEMM / Gram / Kronecker / SOAP
   PK_EW_OTHER = 7,      // other elementwise
-  PK_COUNT = 8
+  PK_PEER_PUSH = 8,     // parameter shards stored into the peers' replicas
+  PK_COUNT = 9
 };
 void count_launch();
 // Records a CUDA event on `st` before (begin) and after (end) a launch when

@@ -24,6 +24,7 @@ _ERRORS = {
     -5: RuntimeError,
     -6: RuntimeError,
     -7: ValueError,
+    -8: RuntimeError,
 }
 
 c_int, c_float, c_size_t, c_void_p = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p
@@ -92,6 +93,11 @@ SIGNATURES: dict[str, tuple] = {
          c_size_t, c_void_p]),
     "lsr_blocks_gather_bf16": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "lsr_blocks_apply_bf16": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_float, c_float, c_void_p]),
+    "lsr_ipc_alloc": (c_int, [c_size_t, ctypes.POINTER(c_void_p), c_void_p]),
+    "lsr_ipc_open": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "lsr_ipc_close": (c_int, [c_void_p]),
+    "lsr_ipc_free": (c_int, [c_void_p]),
+    "lsr_peer_push": (c_int, [c_void_p, c_size_t, ctypes.POINTER(ctypes.c_longlong), c_int, c_int, c_void_p]),
     "lsr_muon_workspace_bytes": (c_size_t, [ctypes.POINTER(MuonGroup), c_int]),
     "lsr_muon_step_bf16": (
         c_int,
@@ -152,7 +158,8 @@ def device_status(clear: bool = True) -> int:
     return code.value
 
 
-PROFILE_KINDS = ("ns_gram", "ns_poly", "ns_update", "orient", "normalize", "apply", "gemm_other", "ew_other")
+PROFILE_KINDS = ("ns_gram", "ns_poly", "ns_update", "orient", "normalize", "apply", "gemm_other", "ew_other",
+                 "peer_push")
 
 
 def launch_count() -> int:

@@ -42,6 +42,7 @@ typedef struct CUstream_st* lsr_stream_t; /* == cudaStream_t */
 #define LSR_ERR_DRIVER (-5)    /* TMA tensor-map encoding failed             */
 #define LSR_ERR_DEVICE (-6)    /* current device is not sm_100               */
 #define LSR_ERR_TOO_LARGE (-7) /* problem exceeds the fixed scratch capacity */
+#define LSR_ERR_PEER (-8)      /* CUDA IPC / peer memory call failed         */
 
 /* Library version string, e.g. "lsr-b200 0.1.0 (sm_100a)". */
 LSR_API const char* lsr_version(void);
@@ -269,6 +270,39 @@ LSR_API int lsr_blocks_gather_bf16(const uint64_t* ptrs, const int* lds, int nbl
                                    void* stack, lsr_stream_t stream);
 LSR_API int lsr_blocks_apply_bf16(const uint64_t* ptrs, const int* lds, int nblocks, int rows, int cols,
                                   const float* U, float lr, float weight_decay, lsr_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Peer-memory exchange of finished parameter shards (sharded Muon step).
+ *
+ * Replaces the exchange step of the distributed paths: the DDP all-reduce
+ * that keeps replicated Muon parameters equal (muon_lm_ddp.py:1270-1278) and
+ * the ZeRO-1 all-gather of DDPDistributedConfig
+ * (shampoo_soap_lm_ddp_zero1.py:341-345). Each rank keeps a replica of every
+ * flat, rank-major parameter buffer in memory the other ranks open through
+ * CUDA IPC; after applying its own updates it stores its shard into every
+ * peer's replica at the same byte offset (lsr_peer_push), then the ranks meet
+ * at a barrier. No counterpart function exists in the reference.
+ *
+ * lsr_ipc_alloc: cudaMalloc `bytes` and export them; `handle` (host) receives
+ *   LSR_IPC_HANDLE_BYTES bytes to send to the other ranks.
+ * lsr_ipc_open / lsr_ipc_close: map / unmap another process's buffer.
+ * lsr_ipc_free: release a buffer made by lsr_ipc_alloc.
+ * lsr_peer_push: for q < npeers store bytes [src, src + bytes) at
+ *   src + peer_deltas[q] (host array; the byte distance from the local buffer
+ *   to peer q's mapped replica, a multiple of 16). `bytes` even; up to
+ *   `max_ctas` CTAs (<= 0: one per SM). The CTAs use no shared memory, so they
+ *   run beside the library's GEMM kernels.
+ * The ipc functions allocate or map memory by design; the push allocates
+ * nothing.
+ * ---------------------------------------------------------------------- */
+#define LSR_IPC_HANDLE_BYTES 64
+#define LSR_MAX_PEERS 15
+LSR_API int lsr_ipc_alloc(size_t bytes, void** ptr, void* handle);
+LSR_API int lsr_ipc_open(const void* handle, void** ptr);
+LSR_API int lsr_ipc_close(void* ptr);
+LSR_API int lsr_ipc_free(void* ptr);
+LSR_API int lsr_peer_push(const void* src, size_t bytes, const long long* peer_deltas, int npeers, int max_ctas,
+                          lsr_stream_t stream);
 
 #ifdef __cplusplus
 }
