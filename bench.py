@@ -575,7 +575,7 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=["lsr", "reference"], default="lsr")
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="GPT-2-XL layers (48 = the full model)")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="nccl",
                     help="N>1: parameter exchange (peer-memory push or NCCL all-gather)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["muon", "cfg1", "cfg2", "cfg3", "cfg5", "muon_torch"], default="muon",

@@ -10,12 +10,13 @@ the momentum update and Newton–Schulz for them.
 Exchange of the results, per shape group, overlapped with the next group's
 Newton–Schulz on the compute stream:
 
-* flat_params with the peer exchange (default on GPUs): every group's
+* flat_params with exchange="peer": every group's
   parameters live in one rank-major buffer in CUDA IPC memory; a rank applies
   its own updates and stores its shard straight into every peer's replica
   (lsr_peer_push, a kernel that runs beside the GEMM kernels), then the ranks
   meet at one barrier per step;
-* flat_params with exchange="nccl": the same layout, in-place NCCL all-gather;
+* flat_params with exchange="nccl" (the default): the same layout, in-place
+  NCCL all-gather;
 * flat_params=False: the oriented bf16 updates are all-gathered with NCCL and
   every rank applies all of them to its own parameter storage.
 
@@ -168,7 +169,7 @@ class ShardedMuon:
 
     def __init__(self, params, lr=0.02, momentum=0.95, nesterov=True, weight_decay=0.01, ns_steps=5, eps=1e-7,
                  lr_adjust="original", process_group=None, engine=None, overlap=True, flat_params=False,
-                 exchange="auto"):
+                 exchange="nccl"):
         self.lr, self.mu, self.nesterov, self.wd = lr, momentum, nesterov, weight_decay
         self.ns_steps, self.eps, self.lr_adjust = ns_steps, eps, lr_adjust
         self.pg = process_group
@@ -197,10 +198,10 @@ class ShardedMuon:
         on_gpu = all(p.is_cuda for G in self.groups for p in G.params)
         self.comm_stream = torch.cuda.Stream() if (self.world > 1 and on_gpu) else None
         self.flat = bool(flat_params) and self.world > 1
-        if exchange not in ("auto", "peer", "nccl"):
-            raise ValueError(f"exchange must be 'auto', 'peer' or 'nccl', got {exchange!r}")
+        if exchange not in ("peer", "nccl"):
+            raise ValueError(f"exchange must be 'peer' or 'nccl', got {exchange!r}")
         self.peer = None
-        if self.flat and on_gpu and exchange in ("auto", "peer"):
+        if self.flat and on_gpu and exchange == "peer":
             if any(G.params[0].dtype != torch.bfloat16 for G in self.groups):
                 raise ValueError("the peer exchange handles bf16 parameters")
             sizes = [local_count(len(G.params), self.world) * self.world * G.params[0].numel() * 2
