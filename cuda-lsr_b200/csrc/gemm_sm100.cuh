@@ -2,9 +2,12 @@
 //
 //   D[g][b] (tile of BM x BN) = sum over segments s of  opA_s[b] * opB_s[b]^T
 //
-// * one CTA per SM (persistent), tiles handed out round-robin over a flat list
-//   that spans up to kMaxGroups independent problem groups (e.g. the four
-//   parameter shapes of a model), each a batch of equally shaped matrices;
+// * one CTA per SM (persistent); tiles of a flat list that spans up to
+//   kMaxGroups independent problem groups (e.g. the four parameter shapes of a
+//   model, each a batch of equally shaped matrices) are claimed dynamically
+//   from a global counter by the producer, which passes each tile index to the
+//   MMA and epilogue warps through a small shared-memory ring; CTAs that start
+//   late (their SM busy with another kernel) simply claim fewer tiles;
 // * warp 0   : TMA producer (one elected thread), STAGES-deep smem ring;
 // * warp 1   : owns TMEM (512 columns = two BN-wide fp32 accumulators) and one
 //              thread issues tcgen05.mma (M=128, N=BN, K=16) per 16-wide K step;
@@ -30,6 +33,7 @@ constexpr int BM = 128;
 constexpr int BK = 64;       // bf16 elements in one 128-byte swizzle row (one K block)
 constexpr int BK_TF32 = 32;  // fp32 (tf32) elements in one 128-byte swizzle row
 constexpr int kGemmThreads = 192;
+constexpr int kTileRing = 8;  // tile indices in flight between the producer and the consumers
 constexpr int kEpiThreads = 128;
 
 // Epilogue modes.
@@ -101,6 +105,7 @@ struct GemmParams {
   int ngroups;
   int total_tiles;
   int* status;
+  unsigned int* sched;  // [0]: next tile to claim, [1]: CTAs finished; both back to 0 when the launch ends
 };
 
 // First column tile of tile row ti touching the upper triangle (tiles of TM x BN).
@@ -144,6 +149,7 @@ enum : int {
   ST_TIMEOUT_MMA_TMEM = 103,
   ST_TIMEOUT_EPILOGUE = 104,
   ST_TIMEOUT_TEARDOWN = 105,
+  ST_TIMEOUT_TILE_QUEUE = 106,
 };
 
 // ---------------------------------------------------------------------------
@@ -560,7 +566,7 @@ struct GemmSmem {
   static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;
   static constexpr int EPI_BYTES = (kEpiThreads / 32) * 4 * EpiT<EPI>::CHB;  // per warp: 2 direct + 2 transposed
   static constexpr int BAR_OFFSET = EPI_OFFSET + EPI_BYTES;
-  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 5) + 16;
+  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 5 + 2 * kTileRing) + 16 + 4 * kTileRing;
   static constexpr int TOTAL = BAR_OFFSET + BAR_BYTES + 1024;  // + alignment slack
 };
 
@@ -606,14 +612,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* done_bar = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  uint64_t* tq_full = done_bar + 1;          // tile ring: slot written
+  uint64_t* tq_empty = tq_full + kTileRing;  // tile ring: slot read by every consumer (leader's barriers)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tq_empty + kTileRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* tile_ring = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
-  const int tile_first = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
-  const int tile_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  // Consumers of one tile-ring slot: the MMA thread and the four epilogue
+  // warps of the leader, plus (pair) the peer's producer and epilogue warps.
+  constexpr uint32_t kTileConsumers = PAIR ? 10u : 5u;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -625,6 +635,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
       mbar_init(tempty + a, kEpiThreads * (PAIR ? 2 : 1));
     }
     mbar_init(done_bar, 1);
+    for (int r = 0; r < kTileRing; ++r) {
+      mbar_init(tq_full + r, 1);
+      mbar_init(tq_empty + r, kTileConsumers);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -656,7 +670,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int t = tile_first; ok && t < p.total_tiles; t += tile_step) {
+      int r = 0;         // tile-ring slot
+      uint32_t rph = 0;  // its phase
+      auto claim = [&]() -> int {
+        const int c = (int)atomicAdd(p.sched, 1u);
+        return c < p.total_tiles ? c : -1;
+      };
+      int t_next = rank == 0 ? claim() : -1;
+      while (ok) {
+        int t;
+        if (rank == 0) {
+          // hand the claimed tile (or the end marker -1) to every consumer
+          if (!mbar_wait(tq_empty + r, rph ^ 1, abort_flag, p.status, ST_TIMEOUT_TILE_QUEUE)) break;
+          t = t_next;
+          tile_ring[r] = t;
+          if constexpr (PAIR) {
+            st_shared_cluster_u32(mapa_shared(smem_u32((const void*)(tile_ring + r)), 1), (uint32_t)t);
+            mbar_arrive_cluster(mapa_shared(smem_u32(tq_full + r), 1));
+          }
+          mbar_arrive(tq_full + r);
+          if (t >= 0) t_next = claim();  // in flight while this tile's loads are issued
+        } else {
+          // pair peer: load the tile the leader claimed
+          if (!mbar_wait_acq_cluster(tq_full + r, rph, abort_flag, p.status, ST_TIMEOUT_TILE_QUEUE)) break;
+          t = tile_ring[r];
+          mbar_arrive_cluster(mapa_shared(smem_u32(tq_empty + r), 0));
+        }
+        if (++r == kTileRing) {
+          r = 0;
+          rph ^= 1;
+        }
+        if (t < 0) break;
         int g, b, ti, tj;
         decode_tile<BN, TM>(p, t, g, b, ti, tj);
         const GroupDesc& G = p.g[g];
@@ -723,7 +767,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
       int acc = 0;
       uint32_t aph = 0;
       bool ok = true;
-      for (int t = tile_first; ok && t < p.total_tiles; t += tile_step) {
+      int r = 0;
+      uint32_t rph = 0;
+      while (ok) {
+        if (!mbar_wait(tq_full + r, rph, abort_flag, p.status, ST_TIMEOUT_TILE_QUEUE)) break;
+        const int t = tile_ring[r];
+        mbar_arrive(tq_empty + r);
+        if (++r == kTileRing) {
+          r = 0;
+          rph ^= 1;
+        }
+        if (t < 0) break;
         int g, b, ti, tj;
         decode_tile<BN, TM>(p, t, g, b, ti, tj);
         const GroupDesc& G = p.g[g];
@@ -817,7 +871,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
     int acc = 0;
     uint32_t aph = 0;
     uint32_t kchunk = 0;  // chunks processed by this warp (staging buffer parity)
-    for (int t = tile_first; t < p.total_tiles; t += tile_step) {
+    int r = 0;
+    uint32_t rph = 0;
+    while (true) {
+      const bool got = (PAIR && rank != 0)
+                           ? mbar_wait_acq_cluster(tq_full + r, rph, abort_flag, p.status, ST_TIMEOUT_TILE_QUEUE)
+                           : mbar_wait(tq_full + r, rph, abort_flag, p.status, ST_TIMEOUT_TILE_QUEUE);
+      if (!got) break;
+      const int t = tile_ring[r];
+      __syncwarp();
+      if (lane == 0) {
+        if (PAIR && rank != 0)
+          mbar_arrive_cluster(mapa_shared(smem_u32(tq_empty + r), 0));
+        else
+          mbar_arrive(tq_empty + r);
+      }
+      if (++r == kTileRing) {
+        r = 0;
+        rph ^= 1;
+      }
+      if (t < 0) break;
       int g, b, ti, tj;
       decode_tile<BN, TM>(p, t, g, b, ti, tj);
       const GroupDesc& G = p.g[g];
@@ -903,6 +976,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
       tmem_dealloc_pair(tmem_base, 512);
     else
       tmem_dealloc(tmem_base, 512);
+  }
+  // The last CTA to finish returns the tile counter to zero for the next
+  // launch that uses this slot (every claim of this launch precedes it).
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned int prev = atomicAdd(p.sched + 1, 1u);
+    if (prev == gridDim.x - 1) {
+      atomicExch(p.sched, 0u);
+      atomicExch(p.sched + 1, 0u);
+    }
   }
 }
 

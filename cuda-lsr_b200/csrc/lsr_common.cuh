@@ -159,6 +159,41 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// Store a 32-bit value at a shared::cluster address (possibly in the peer CTA).
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
+// try_wait with cluster-scope acquire: observes shared-memory writes that the
+// peer CTA released with mbarrier.arrive.release.cluster on this barrier.
+__device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait as mbar_wait, with cluster-scope acquire.
+__device__ __forceinline__ bool mbar_wait_acq_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                      int* status, int code) {
+  if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > LSR_WAIT_TIMEOUT_NS) {
+      set_status(status, code);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
 // Arrive on an mbarrier given by its shared::cluster address (possibly in the peer CTA).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");

@@ -14,9 +14,19 @@ namespace lsr {
 // kernel recorded (e.g. a bounded wait that timed out).
 __device__ int g_status_word;
 
+// Tile counters of the GEMM engine's dynamic scheduler: two words per launch
+// slot, zero between launches (the last CTA of each launch resets its slot).
+// Launches take slots round-robin, so launches running at the same time (on
+// different streams) use different counters as long as fewer than
+// kSchedSlots are in flight.
+constexpr int kSchedSlots = 1024;
+__device__ unsigned int g_tile_sched[2 * kSchedSlots];
+
 namespace {
 constexpr int kMaxDevices = 64;
 int* g_status_cache[kMaxDevices] = {nullptr};
+unsigned int* g_sched_cache[kMaxDevices] = {nullptr};
+std::atomic<unsigned int> g_sched_next{0};
 int g_sm_cache[kMaxDevices] = {0};
 int g_cc_cache[kMaxDevices] = {0};
 
@@ -87,6 +97,18 @@ int* status_ptr() {
     g_status_cache[d] = static_cast<int*>(p);
   }
   return g_status_cache[d];
+}
+
+unsigned int* sched_slot() {
+  const int d = current_device();
+  if (d < 0) return nullptr;
+  if (!g_sched_cache[d]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_tile_sched) != cudaSuccess) return nullptr;
+    g_sched_cache[d] = static_cast<unsigned int*>(p);
+  }
+  const unsigned int k = g_sched_next.fetch_add(1, std::memory_order_relaxed) % kSchedSlots;
+  return g_sched_cache[d] + 2 * k;
 }
 
 int device_sm_count() {

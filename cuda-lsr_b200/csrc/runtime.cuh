@@ -12,6 +12,9 @@ namespace lsr {
 
 // Status word of the current device (device pointer), or nullptr on failure.
 int* status_ptr();
+// Two zeroed tile counters of the GEMM engine's dynamic scheduler for one
+// launch on the current device (nullptr on failure).
+unsigned int* sched_slot();
 // Number of SMs of the current device.
 int device_sm_count();
 // LSR_OK if the current device is sm_100 (B200 class).
@@ -146,7 +149,8 @@ inline int launch_gemm(GemmParams& p, cudaStream_t st, int kind = PK_GEMM_OTHER)
   if (p.total_tiles == 0) return LSR_OK;
   for (int g = 0; g < p.ngroups; ++g) setup_out_map<EPI>(p, g);
   p.status = status_ptr();
-  if (!p.status) return LSR_ERR_LAUNCH;
+  p.sched = sched_slot();
+  if (!p.status || !p.sched) return LSR_ERR_LAUNCH;
   auto kfn = gemm_sm100_kernel<BN, STAGES, EPI, TF32, DUAL, PAIR>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL) != cudaSuccess)
     return LSR_ERR_LAUNCH;
