@@ -24,6 +24,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -429,6 +430,31 @@ def _time_cpu(fn, reps=2):
     return statistics.median(t)
 
 
+def _torch_batched_coupled_newton(A, root, tolerance=1e-6, max_iterations=100):
+    """The reference's batched recurrence (shampoo.py:408-542) as plain torch fp32 ops."""
+    B, n, _ = A.shape
+    eye = torch.eye(n, device=A.device, dtype=A.dtype).expand(B, n, n)
+    alpha = -1.0 / float(root)
+    z = (root + 1.0) / (2.0 * A.flatten(1).norm(dim=1))
+    X = (z.pow(-alpha)[:, None, None] * eye).contiguous()
+    M = (z[:, None, None] * A).contiguous()
+    active = (M - eye).abs().flatten(1).amax(dim=1) > tolerance
+    for _ in range(max_iterations):
+        if not bool(active.any()):
+            break
+        Mp = alpha * M + (1.0 - alpha) * eye
+        Xn = X @ Mp
+        P = Mp @ Mp
+        if root == 4:
+            P = P @ P
+        Mn = P @ M
+        m3 = active[:, None, None]
+        X = torch.where(m3, Xn, X)
+        M = torch.where(m3, Mn, M)
+        active = (M - eye).abs().flatten(1).amax(dim=1) > tolerance
+    return X
+
+
 def run_workload(args) -> None:
     import lsr
     import lsr.kron as K
@@ -525,6 +551,35 @@ def run_workload(args) -> None:
                                       f"{sum(len(grp.refs) for _, grp, _ in opt._groups)} blocks at 1024, 1 GPU",
                           "value": ms, "unit": "ms", "algorithmic_tflop": fl / 1e12, "tflops": fl / ms / 1e9,
                           "frac_of_sustained": fl / ms / 1e9 / peaks["bf16_tflops_sustained"]})
+    elif w == "f1":
+        # Batched coupled Newton inverse roots on the reference's full bucket list
+        # (shampoo.py:812-840: (n, root, B), seeds 17 + 100 j, tolerance 1e-6,
+        # max 100 iterations), SPD factors built as make_spd_batch builds them.
+        # Beside ours: the reference's batched op sequence in torch fp32 (TF32
+        # off, cuBLAS SGEMM, shampoo.py:408-542) on the same GPU.
+        torch.backends.cuda.matmul.allow_tf32 = False
+        buckets = [(128, 4, 2), (256, 2, 86), (256, 4, 128), (512, 2, 128), (512, 4, 128)]
+        tot_ours = tot_ref = 0.0
+        for j, (n, root, B) in enumerate(buckets):
+            g = torch.Generator().manual_seed(17 + 100 * j)
+            Xr = torch.randn(B, n, n, generator=g)
+            A = Xr @ Xr.transpose(-1, -2) / float(n)
+            A = A / A.flatten(1).norm(dim=1).clamp_min(1e-12)[:, None, None] * math.sqrt(n)
+            ridge = torch.full((B,), 1e-2)
+            ridge[-max(1, int(round(B * 0.15))):] = 1e-5
+            A = (A + ridge[:, None, None] * torch.eye(n)).contiguous().to(dev)
+            _, iters, _ = lsr.batched_coupled_newton(A, root)
+            ms = _time_gpu(lambda: lsr.batched_coupled_newton(A, root), args.warmup, args.steps)
+            ms_ref = _time_gpu(lambda: _torch_batched_coupled_newton(A, root), 1, max(1, args.steps // 2))
+            fl = float(iters.sum().item()) * (3 if root == 2 else 4) * 2.0 * n ** 3
+            tot_ours += ms
+            tot_ref += ms_ref
+            lines.append({"workload": f"f1: batched coupled Newton n={n} root={root} B={B}", "value": ms,
+                          "unit": "ms", "torch_fp32_ms": ms_ref, "speedup_vs_torch_fp32": ms_ref / ms,
+                          "iters_median": float(iters.float().median().item()), "iters_max": int(iters.max().item()),
+                          "algorithmic_tflop": fl / 1e12, "tflops": fl / ms / 1e9})
+        lines.append({"workload": "f1: all five buckets", "value": tot_ours, "unit": "ms",
+                      "torch_fp32_ms": tot_ref, "speedup_vs_torch_fp32": tot_ref / tot_ours})
     elif w == "muon_torch":
         # The reference's Muon op sequence (muon_lm_ddp.py:554-593, :373-426: momentum,
         # torch.bmm Newton-Schulz per shape group in chunks of 8, apply) on this GPU
@@ -578,7 +633,7 @@ def main(argv=None) -> int:
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="nccl",
                     help="N>1: parameter exchange (peer-memory push or NCCL all-gather)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["muon", "cfg1", "cfg2", "cfg3", "cfg5", "muon_torch"], default="muon",
+    ap.add_argument("--workload", choices=["muon", "cfg1", "cfg2", "cfg3", "cfg5", "f1", "muon_torch"], default="muon",
                     help="muon = the headline GPT-2-XL Muon step (default); cfgN = per-row workloads")
     args = ap.parse_args(argv)
     if args.workload != "muon" and args.impl == "lsr":

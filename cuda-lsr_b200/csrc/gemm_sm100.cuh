@@ -94,6 +94,7 @@ struct GroupDesc {
   float* st_m;  // EPI_SOAP_ADAM: first / second moments (fp32, same layout as out)
   float* st_v;
   float b1, b2, c1, c2, eps;  // EPI_SOAP_ADAM scalars (c1, c2: bias corrections 1/(1-b^t))
+  const int* active;  // optional per-batch-entry flags: tiles of entries whose flag is 0 are skipped
 };
 
 struct GemmParams {
@@ -106,6 +107,7 @@ struct GemmParams {
   int total_tiles;
   int* status;
   unsigned int* sched;  // [0]: next tile to claim, [1]: CTAs finished; both back to 0 when the launch ends
+  int masked;           // some group has `active` flags
 };
 
 // First column tile of tile row ti touching the upper triangle (tiles of TM x BN).
@@ -229,17 +231,29 @@ __device__ __forceinline__ void epilogue_chunk(const GroupDesc& G, int b, int ro
   } else if constexpr (EPI == EPI_SPLIT_BF16X2 || EPI == EPI_SPLIT_TF32) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      if (j >= ncols) continue;
+      if (j < lo || j >= ncols) continue;
       const long long idx = (long long)b * G.out_bs +
                             (G.out_trans ? (long long)(col0 + j) * G.ldo + row : (long long)row * G.ldo + col0 + j);
+      // symmetric output: the mirrored element too
+      const bool mir = G.tri && col0 + j > row;
+      const long long midx = (long long)b * G.out_bs + (long long)(col0 + j) * G.ldo + row;
       if constexpr (EPI == EPI_SPLIT_TF32) {
         const float h = tf32_hi(v[j]);
         reinterpret_cast<float*>(G.out)[idx] = h;
         reinterpret_cast<float*>(G.out2)[idx] = v[j] - h;
+        if (mir) {
+          reinterpret_cast<float*>(G.out)[midx] = h;
+          reinterpret_cast<float*>(G.out2)[midx] = v[j] - h;
+        }
       } else {
         const __nv_bfloat16 h = __float2bfloat16_rn(v[j]);
+        const __nv_bfloat16 l = __float2bfloat16_rn(v[j] - __bfloat162float(h));
         reinterpret_cast<__nv_bfloat16*>(G.out)[idx] = h;
-        reinterpret_cast<__nv_bfloat16*>(G.out2)[idx] = __float2bfloat16_rn(v[j] - __bfloat162float(h));
+        reinterpret_cast<__nv_bfloat16*>(G.out2)[idx] = l;
+        if (mir) {
+          reinterpret_cast<__nv_bfloat16*>(G.out)[midx] = h;
+          reinterpret_cast<__nv_bfloat16*>(G.out2)[midx] = l;
+        }
       }
     }
     return;
@@ -499,6 +513,32 @@ __device__ __forceinline__ void epilogue_chunk_staged(const GemmParams& p, int g
       tma_store_3d(&p.mapOut2[g], tbuf, col0, row0, b);
       bulk_commit();
     }
+    if (G.tri && col0 > row0) {
+      // symmetric output: the mirrored chunk goes out from the same buffers
+      // once the TMA engine has read them
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const uint32_t off = stg_off<T::ROWB>(j, (lane * T::ESZ) / 16) + (lane * T::ESZ) % 16;
+        if constexpr (T::F32) {
+          const float h = tf32_hi(v[j]);
+          *reinterpret_cast<float*>(dbuf + off) = h;
+          *reinterpret_cast<float*>(tbuf + off) = v[j] - h;
+        } else {
+          const __nv_bfloat16 h = __float2bfloat16_rn(v[j]);
+          *reinterpret_cast<__nv_bfloat16*>(dbuf + off) = h;
+          *reinterpret_cast<__nv_bfloat16*>(tbuf + off) = __float2bfloat16_rn(v[j] - __bfloat162float(h));
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_3d(&p.mapOut[g], dbuf, row0, col0, b);
+        tma_store_3d(&p.mapOut2[g], tbuf, row0, col0, b);
+        bulk_commit();
+      }
+    }
     return;
   }
   const bool diag = G.tri && col0 == row0;
@@ -673,8 +713,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
       int r = 0;         // tile-ring slot
       uint32_t rph = 0;  // its phase
       auto claim = [&]() -> int {
-        const int c = (int)atomicAdd(p.sched, 1u);
-        return c < p.total_tiles ? c : -1;
+        while (true) {
+          const int c = (int)atomicAdd(p.sched, 1u);
+          if (c >= p.total_tiles) return -1;
+          if (!p.masked) return c;
+          int g, b, ti, tj;
+          decode_tile<BN, TM>(p, c, g, b, ti, tj);
+          const int* act = p.g[g].active;
+          if (!act || *reinterpret_cast<const volatile int*>(act + b)) return c;
+        }
       };
       int t_next = rank == 0 ? claim() : -1;
       while (ok) {

@@ -93,6 +93,10 @@ SIGNATURES: dict[str, tuple] = {
          c_size_t, c_void_p]),
     "lsr_blocks_gather_bf16": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "lsr_blocks_apply_bf16": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_float, c_float, c_void_p]),
+    "lsr_coupled_newton_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "lsr_coupled_newton_f32": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float, c_int,
+                c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "lsr_ipc_alloc": (c_int, [c_size_t, ctypes.POINTER(c_void_p), c_void_p]),
     "lsr_ipc_open": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
     "lsr_ipc_close": (c_int, [c_void_p]),

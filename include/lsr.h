@@ -272,6 +272,37 @@ LSR_API int lsr_blocks_apply_bf16(const uint64_t* ptrs, const int* lds, int nblo
                                   const float* U, float lr, float weight_decay, lsr_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Batched coupled Newton inverse roots  X[b] = (A[b] + eps I)^{-1/root}
+ *
+ * Replaces batched_coupled_newton (shampoo.py:408-542; the recurrence of
+ * coupled_newton_one, shampoo.py:277-347): fp32 SPD factors A [batch][n][n],
+ * root 2 or 4, per-factor convergence mask (a factor stops when
+ * max|M - I| <= tolerance or after max_iterations). Outputs X fp32
+ * [batch][n][n], iters int32 [batch] (iterations each factor ran), err fp32
+ * [batch] (its final max|M - I|). n a multiple of 4; A, X 16-byte aligned.
+ * use_tf32 = 0 (the reference runs with TF32 off): the recurrence in fp32
+ * FFMA on the CUDA cores, the reference's numerics (symmetric products
+ * computed as upper triangles and mirrored). use_tf32 = 1: the products run
+ * as 3xTF32 on the tensor cores until max|M - I| <= 1e-4, then in fp32
+ * FFMA to the tolerance (X then within ~1e-4 of the fp32 result on
+ * well-conditioned factors); factors that needed more than
+ * 14 (root 2) / 13 (root 4) iterations (ill-conditioned ones, where the
+ * tensor cores' truncating accumulation costs accuracy) are then recomputed
+ * from scratch in fp32 FFMA, as the reference's hybrid path recomputes its
+ * hard factors (shampoo.py:545-595), and redo (int32 [batch], may be NULL)
+ * receives 1 for them. iters counts the recurrence's iterations, err is the
+ * final max|M - I|.
+ * check_every = k > 0: every k iterations
+ * the host reads the number of active factors (a stream synchronization) and
+ * stops when it is 0; check_every = 0: no host synchronization, always
+ * max_iterations rounds of launches (converged factors skip all work).
+ * ---------------------------------------------------------------------- */
+LSR_API size_t lsr_coupled_newton_workspace_bytes(int batch, int n);
+LSR_API int lsr_coupled_newton_f32(const float* A, float* X, int* iters, float* err, int* redo, int batch, int n,
+                                   int root, float epsilon, float tolerance, int max_iterations, int check_every,
+                                   int use_tf32, void* ws, size_t ws_bytes, lsr_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Peer-memory exchange of finished parameter shards (sharded Muon step).
  *
  * Replaces the exchange step of the distributed paths: the DDP all-reduce

@@ -58,3 +58,31 @@ def muon_step_torch(params, grads, moms, lr, mu, nesterov, wd, ns_steps, eps, lr
         if wd != 0.0:
             p.mul_(1.0 - lr * wd)
         p.add_(o.to(dtype=p.dtype), alpha=-adjusted_lr(lr, p.shape, lr_adjust))
+
+
+def batched_coupled_newton_torch(A, root, tolerance=1e-6, max_iterations=100):
+    """The reference's batched coupled Newton recurrence (shampoo.py:408-542) as
+    plain torch ops in A's dtype and device (fp32 reference numerics on CPU)."""
+    B, n, _ = A.shape
+    eye = torch.eye(n, device=A.device, dtype=A.dtype).expand(B, n, n)
+    alpha = -1.0 / float(root)
+    z = (root + 1.0) / (2.0 * A.flatten(1).norm(dim=1))
+    X = (z.pow(-alpha)[:, None, None] * eye).contiguous()
+    M = (z[:, None, None] * A).contiguous()
+    iters = torch.zeros(B, dtype=torch.int32, device=A.device)
+    active = (M - eye).abs().flatten(1).amax(dim=1) > tolerance
+    for _ in range(max_iterations):
+        if not bool(active.any()):
+            break
+        Mp = alpha * M + (1.0 - alpha) * eye
+        Xn = X @ Mp
+        P = Mp @ Mp
+        if root == 4:
+            P = P @ P
+        Mn = P @ M
+        m3 = active[:, None, None]
+        X = torch.where(m3, Xn, X)
+        M = torch.where(m3, Mn, M)
+        iters = iters + active.to(torch.int32)
+        active = (M - eye).abs().flatten(1).amax(dim=1) > tolerance
+    return X, iters

@@ -13,7 +13,11 @@ code on CPU (run in a container where the cuda-lsr checkout is mounted):
 * kronrec_golden.npz — batched_kron / vectorized_kron of kron_cuda.py:117-145,
                       :618-629 on K = 5 / 4 / 3 factor sets (same extraction).
 * newton_golden.npz — coupled_newton_one (+ matrix_power_small) of shampoo.py:254-347
-                      (same extraction).
+                      (same extraction), and batched_coupled_newton (:408-542) on
+                      SPD batches built as make_spd_batch (:178-247) builds them
+                      (Gram / n, Frobenius norm sqrt(n), ridge 1e-2 with a 15%
+                      tail at 1e-5): outputs, per-factor iteration counts and
+                      final errors.
 
 Inputs are seeded torch CPU draws; bf16 arrays are stored as uint16 bit
 patterns, fp32 arrays as float32. The fixtures hold inputs and outputs, so the
@@ -180,6 +184,26 @@ def make_newton(ref: Path) -> dict:
             res = fns["coupled_newton_one"](A, root=root)
             X = res[0] if isinstance(res, tuple) else res
             out[f"newton{i}_root{root}"] = X.numpy()
+    # batched, per-factor convergence mask
+    env_b = {"torch": torch, "math": math, "DEV": "cpu"}
+    fb = extract_functions(ref / "shampoo.py", ["matrix_power_small", "coupled_newton_one", "batched_coupled_newton"],
+                           env_b)
+    for j, (n, B, roots) in enumerate([(48, 7, (2, 4)), (96, 2, (4,))]):
+        g = torch.Generator().manual_seed(2024 + j)
+        Xr = torch.randn(B, n, n, generator=g)
+        A = Xr @ Xr.transpose(-1, -2) / float(n)
+        A = A / A.flatten(1).norm(dim=1).clamp_min(1e-12)[:, None, None] * math.sqrt(n)
+        ridge = torch.full((B,), 1e-2)
+        ridge[-max(1, int(round(B * 0.15))):] = 1e-5
+        A = (A + ridge[:, None, None] * torch.eye(n)).contiguous()
+        out[f"nbatch{j}_A"] = A.numpy()
+        for root in roots:
+            X, iters, err = fb["batched_coupled_newton"](A, root=root)
+            out[f"nbatch{j}_root{root}_X"] = X.numpy()
+            out[f"nbatch{j}_root{root}_iters"] = iters.numpy()
+            out[f"nbatch{j}_root{root}_err"] = err.numpy()
+            out[f"nbatch{j}_root{root}_iters_one"] = np.array(
+                [fb["coupled_newton_one"](A[b], root=root)[1] for b in range(B)], dtype=np.int32)
     return out
 
 
