@@ -559,7 +559,7 @@ def run_workload(args) -> None:
         # off, cuBLAS SGEMM, shampoo.py:408-542) on the same GPU.
         torch.backends.cuda.matmul.allow_tf32 = False
         buckets = [(128, 4, 2), (256, 2, 86), (256, 4, 128), (512, 2, 128), (512, 4, 128)]
-        tot_ours = tot_ref = 0.0
+        tot_ours = tot_ref = tot_tc = 0.0
         for j, (n, root, B) in enumerate(buckets):
             g = torch.Generator().manual_seed(17 + 100 * j)
             Xr = torch.randn(B, n, n, generator=g)
@@ -571,15 +571,20 @@ def run_workload(args) -> None:
             _, iters, _ = lsr.batched_coupled_newton(A, root)
             ms = _time_gpu(lambda: lsr.batched_coupled_newton(A, root), args.warmup, args.steps)
             ms_ref = _time_gpu(lambda: _torch_batched_coupled_newton(A, root), 1, max(1, args.steps // 2))
+            from lsr import newton as NW
+            ms_tc = _time_gpu(lambda: NW._run(A, root, 0.0, 1e-6, 100, use_tf32=True), args.warmup, args.steps)
             fl = float(iters.sum().item()) * (3 if root == 2 else 4) * 2.0 * n ** 3
             tot_ours += ms
             tot_ref += ms_ref
+            tot_tc += ms_tc
             lines.append({"workload": f"f1: batched coupled Newton n={n} root={root} B={B}", "value": ms,
                           "unit": "ms", "torch_fp32_ms": ms_ref, "speedup_vs_torch_fp32": ms_ref / ms,
+                          "tf32_mode_ms": ms_tc,
                           "iters_median": float(iters.float().median().item()), "iters_max": int(iters.max().item()),
                           "algorithmic_tflop": fl / 1e12, "tflops": fl / ms / 1e9})
         lines.append({"workload": "f1: all five buckets", "value": tot_ours, "unit": "ms",
-                      "torch_fp32_ms": tot_ref, "speedup_vs_torch_fp32": tot_ref / tot_ours})
+                      "torch_fp32_ms": tot_ref, "speedup_vs_torch_fp32": tot_ref / tot_ours, "tf32_mode_ms": tot_tc,
+                      "note": "value: fp32 FFMA (the reference's precision); tf32_mode_ms: TF32 allowed"})
     elif w == "muon_torch":
         # The reference's Muon op sequence (muon_lm_ddp.py:554-593, :373-426: momentum,
         # torch.bmm Newton-Schulz per shape group in chunks of 8, apply) on this GPU

@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(CN_THREADS) cn_norm_kernel(const float* __rest
 }
 
 // Start of the recurrence for every factor with sel[b] (all when sel is null):
-// X = z^{1/p} I, M = z (A + eps I), as fp32 into X / M, or as tf32 pairs into
+// X = z^{1/p} I, M = z (sym(A) + eps I), as fp32 into X / M, or as tf32 pairs into
 // Xh / Xl, Mh / Ml when Xh is given; errb = max |M - I|.
 __global__ void __launch_bounds__(CN_THREADS) cn_init_kernel(const float* __restrict__ A, int n, float eps, int root,
                                                             const float* __restrict__ z, const int* __restrict__ sel,
@@ -142,7 +142,16 @@ __global__ void __launch_bounds__(CN_THREADS) cn_init_kernel(const float* __rest
   const float xd = powf(zb, 1.f / (float)root);
   float m = 0.f;
   CN_FOR_ELEMS(k) {
+    // the symmetric part of A (A itself when A is exactly symmetric): every
+    // product of the recurrence then has symmetric operands
     float4 a = reinterpret_cast<const float4*>(A)[base + k];
+    {
+      const long long e = 4 * k;
+      const int r = (int)(e / n), c = (int)(e % n);
+      const float* At = A + (long long)b * n * n;
+      a = make_float4(0.5f * (a.x + At[(long long)c * n + r]), 0.5f * (a.y + At[(long long)(c + 1) * n + r]),
+                      0.5f * (a.z + At[(long long)(c + 2) * n + r]), 0.5f * (a.w + At[(long long)(c + 3) * n + r]));
+    }
     if (eps != 0.f) a = add4(a, diag4(4 * k, n, eps));
     const float4 mm = make_float4(__fmul_rn(zb, a.x), __fmul_rn(zb, a.y), __fmul_rn(zb, a.z), __fmul_rn(zb, a.w));
     const float4 x = diag4(4 * k, n, xd);
@@ -307,16 +316,31 @@ int cn_tc_products(int ng, float* const* outh, float* const* outl, const float* 
 // Passes 2 and 3: fp32 FFMA on the CUDA cores
 // ---------------------------------------------------------------------------
 
-constexpr int SG_T = 128;  // output tile (SG_T x SG_T per block)
-constexpr int SG_K = 8;    // K step
+constexpr int SG_T = 128;    // output tile (SG_T x SG_T per block)
+constexpr int SG_K = 16;     // K rows per pipeline stage
+constexpr int SG_STAGES = 3;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
+  const uint32_t s = smem_u32(smem);
+  const int n = pred ? 16 : 0;  // 0: the 16 bytes are zero-filled
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 // C[b] = A[b] B[b] for every factor with active[b] (n x n row-major fp32,
-// n % 4 == 0), a symmetric product: only tiles on or above the diagonal run and
-// mirror their elements. 256 threads, each 8 x 8 outputs (two 4-row by two
-// 4-column strips 64 apart), fp32 FFMA in K order, summed per 8-wide K step
-// before it enters the running sum; A and B tiles double-buffered
-// in shared memory (A transposed), the next tile's loads in flight while the
-// current one is multiplied.
+// n % 4 == 0), for a symmetric A and a symmetric product (every product of the
+// recurrence: its operands are polynomials in the same factor). A symmetric
+// means the A tile's K-major copy is A's own rows, so both tiles are plain
+// 16-byte cp.async copies into a 3-stage shared-memory ring. Only tiles on or
+// above the diagonal run, and mirror their elements. 256 threads = 8 warps of
+// 32 x 64 outputs (4 x 2 warps per tile); a lane owns 8 x 8 outputs, two 4-row
+// strips 16 apart by two 4-column strips 32 apart. fp32 FFMA in K order,
+// summed per 8-wide K step before it enters the running sum (n / 8 roundings
+// of the running sum instead of n).
 __global__ void __launch_bounds__(256) cn_sgemm_kernel(const float* __restrict__ A, const float* __restrict__ B,
                                                       float* __restrict__ C, int n, const int* __restrict__ active) {
   const int b = blockIdx.z;
@@ -325,68 +349,66 @@ __global__ void __launch_bounds__(256) cn_sgemm_kernel(const float* __restrict__
   A += off;
   B += off;
   C += off;
-  __shared__ __align__(16) float As[2][SG_K][SG_T];
-  __shared__ __align__(16) float Bs[2][SG_K][SG_T];
+  __shared__ __align__(16) float As[SG_STAGES][SG_K][SG_T];  // As[k][r] = A[k0 + k][r0 + r] = A[r0 + r][k0 + k]
+  __shared__ __align__(16) float Bs[SG_STAGES][SG_K][SG_T];  // Bs[k][c] = B[k0 + k][c0 + c]
   const int r0 = blockIdx.y * SG_T, c0 = blockIdx.x * SG_T;
   const int tid = threadIdx.x;
-  const int tx = tid & 15, ty = tid >> 4;
-  // loaders: A tile SG_T rows x 8 k (a float4 of k per thread), B tile 8 k x SG_T cols
-  const int ar = tid >> 1, ak = (tid & 1) * 4;
-  const int bk = tid >> 5, bc = (tid & 31) * 4;
-  auto load = [&](int k0, float4& av, float4& bv) {
-    av = make_float4(0.f, 0.f, 0.f, 0.f);
-    bv = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (r0 + ar < n && k0 + ak < n) av = *reinterpret_cast<const float4*>(A + (long long)(r0 + ar) * n + k0 + ak);
-    if (k0 + bk < n && c0 + bc < n) bv = *reinterpret_cast<const float4*>(B + (long long)(k0 + bk) * n + c0 + bc);
-  };
-  auto store = [&](int buf, const float4& av, const float4& bv) {
-    As[buf][ak + 0][ar] = av.x;
-    As[buf][ak + 1][ar] = av.y;
-    As[buf][ak + 2][ar] = av.z;
-    As[buf][ak + 3][ar] = av.w;
-    *reinterpret_cast<float4*>(&Bs[buf][bk][bc]) = bv;
-  };
-  float acc[8][8] = {};
-  float4 av, bv;
-  load(0, av, bv);
-  store(0, av, bv);
-  __syncthreads();
-  int buf = 0;
-  for (int k0 = 0; k0 < n; k0 += SG_K) {
-    const bool more = k0 + SG_K < n;
-    if (more) load(k0 + SG_K, av, bv);
-    // the 8 products of this K step are summed on their own, then added:
-    // the running sum takes n / 8 roundings instead of n
-    float part[8][8];
+  const int lane = tid & 31, warp = tid >> 5;
+  const int rbase = (warp >> 1) * 32 + (lane >> 3) * 4;  // first of the lane's rows (then +16)
+  const int cbase = (warp & 1) * 64 + (lane & 7) * 4;    // first of the lane's columns (then +32)
+  // copy K rows [k0, k0 + 16) of both tiles into stage s: 512 16-byte vectors each, 2 per thread
+  auto issue = [&](int s, int k0) {
 #pragma unroll
-    for (int k = 0; k < SG_K; ++k) {
-      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][k][ty * 4]);
-      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][k][ty * 4 + 64]);
-      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 4]);
-      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 4 + 64]);
-      const float a8[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      const float b8[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    for (int t = 0; t < 2; ++t) {
+      const int v = tid + t * 256;
+      const int kr = v >> 5, cv = (v & 31) * 4;
+      const int gk = k0 + kr;
+      const bool ka = gk < n;
+      cp_async16(&As[s][kr][cv], A + (long long)(ka ? gk : 0) * n + (r0 + cv < n ? r0 + cv : 0), ka && r0 + cv < n);
+      cp_async16(&Bs[s][kr][cv], B + (long long)(ka ? gk : 0) * n + (c0 + cv < n ? c0 + cv : 0), ka && c0 + cv < n);
+    }
+  };
+  const int ksteps = (n + SG_K - 1) / SG_K;
+  issue(0, 0);
+  cp_async_commit();
+  if (ksteps > 1) issue(1, SG_K);
+  cp_async_commit();
+  float acc[8][8] = {};
+  for (int ks = 0; ks < ksteps; ++ks) {
+    cp_async_wait<1>();  // stage ks has landed (this thread's copies)
+    __syncthreads();     // ... and every thread's; stage ks - 1 is no longer read
+    if (ks + 2 < ksteps) issue((ks + 2) % SG_STAGES, (ks + 2) * SG_K);
+    cp_async_commit();
+    const int s = ks % SG_STAGES;
+#pragma unroll
+    for (int h = 0; h < SG_K; h += 8) {
+      float part[8][8];
+#pragma unroll
+      for (int k = h; k < h + 8; ++k) {
+        const float4 a0 = *reinterpret_cast<const float4*>(&As[s][k][rbase]);
+        const float4 a1 = *reinterpret_cast<const float4*>(&As[s][k][rbase + 16]);
+        const float4 b0 = *reinterpret_cast<const float4*>(&Bs[s][k][cbase]);
+        const float4 b1 = *reinterpret_cast<const float4*>(&Bs[s][k][cbase + 32]);
+        const float a8[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const float b8[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) part[i][j] = k == h ? a8[i] * b8[j] : fmaf(a8[i], b8[j], part[i][j]);
+      }
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) part[i][j] = k == 0 ? a8[i] * b8[j] : fmaf(a8[i], b8[j], part[i][j]);
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[i][j] += part[i][j];
-    if (more) {
-      store(buf ^ 1, av, bv);
-      __syncthreads();
-      buf ^= 1;
+        for (int j = 0; j < 8; ++j) acc[i][j] += part[i][j];
     }
   }
+  cp_async_wait<0>();
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const int r = r0 + ty * 4 + (i & 3) + (i >> 2) * 64;
+    const int r = r0 + rbase + (i & 3) + (i >> 2) * 16;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int c = c0 + tx * 4 + (j & 3) + (j >> 2) * 64;
+      const int c = c0 + cbase + (j & 3) + (j >> 2) * 32;
       if (r >= n || c >= n || c < r) continue;
       C[(long long)r * n + c] = acc[i][j];
       if (c > r) C[(long long)c * n + r] = acc[i][j];
