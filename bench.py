@@ -561,6 +561,8 @@ def run_workload(args) -> None:
         buckets = [(128, 4, 2), (256, 2, 86), (256, 4, 128), (512, 2, 128), (512, 4, 128)]
         tot_ours = tot_ref = tot_tc = 0.0
         for j, (n, root, B) in enumerate(buckets):
+            if args.bucket is not None and j != args.bucket:
+                continue
             g = torch.Generator().manual_seed(17 + 100 * j)
             Xr = torch.randn(B, n, n, generator=g)
             A = Xr @ Xr.transpose(-1, -2) / float(n)
@@ -582,9 +584,10 @@ def run_workload(args) -> None:
                           "tf32_mode_ms": ms_tc,
                           "iters_median": float(iters.float().median().item()), "iters_max": int(iters.max().item()),
                           "algorithmic_tflop": fl / 1e12, "tflops": fl / ms / 1e9})
-        lines.append({"workload": "f1: all five buckets", "value": tot_ours, "unit": "ms",
-                      "torch_fp32_ms": tot_ref, "speedup_vs_torch_fp32": tot_ref / tot_ours, "tf32_mode_ms": tot_tc,
-                      "note": "value: fp32 FFMA (the reference's precision); tf32_mode_ms: TF32 allowed"})
+        if args.bucket is None:
+          lines.append({"workload": "f1: all five buckets", "value": tot_ours, "unit": "ms",
+                        "torch_fp32_ms": tot_ref, "speedup_vs_torch_fp32": tot_ref / tot_ours, "tf32_mode_ms": tot_tc,
+                        "note": "value: fp32 FFMA (the reference's precision); tf32_mode_ms: TF32 allowed"})
     elif w == "muon_torch":
         # The reference's Muon op sequence (muon_lm_ddp.py:554-593, :373-426: momentum,
         # torch.bmm Newton-Schulz per shape group in chunks of 8, apply) on this GPU
@@ -635,6 +638,7 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=["lsr", "reference"], default="lsr")
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="GPT-2-XL layers (48 = the full model)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--bucket", type=int, default=None, help="f1 workload: run one bucket (0..4) only")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="nccl",
                     help="N>1: parameter exchange (peer-memory push or NCCL all-gather)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
