@@ -563,13 +563,20 @@ size_t muon_carve(const lsr_muon_group* groups, int ngroups, uint8_t* ws, std::v
 
 // Momentum + orientation + normalisation + NS for all groups; results land in
 // G.final_out when set, else in G.X[steps & 1].
+// phase bit 1: momentum / orientation / normalisation into the workspace;
+// phase bit 2: Newton–Schulz iterations from the workspace into the outputs.
 int muon_orthogonalize(const lsr_muon_group* groups, int ngroups, std::vector<NsGroup>& gs, float mu, int nesterov,
-                       int steps, float a, float b, float c, float eps, cudaStream_t st) {
+                       int steps, float a, float b, float c, float eps, cudaStream_t st, int phase = 3) {
   std::vector<NsGroup> live;
   std::vector<int> live_idx;
   for (int i = 0; i < ngroups; ++i) {
     const lsr_muon_group& g = groups[i];
     if (g.count == 0) continue;
+    if (!(phase & 1)) {
+      live.push_back(gs[i]);
+      live_idx.push_back(i);
+      continue;
+    }
     if (!g.grad_ptrs || !g.mom_ptrs) return LSR_ERR_ARG;
     const MuonShape s = muon_shape(g);
     NsGroup& G = gs[i];
@@ -584,6 +591,7 @@ int muon_orthogonalize(const lsr_muon_group* groups, int ngroups, std::vector<Ns
     live.push_back(G);
     live_idx.push_back(i);
   }
+  if (!(phase & 2)) return LSR_OK;
   if (steps == 0) {
     for (size_t k = 0; k < live.size(); ++k) {
       NsGroup& G = live[k];
@@ -726,6 +734,14 @@ int lsr_muon_step_bf16(const lsr_muon_group* groups, int ngroups, float momentum
 int lsr_muon_orthogonalize_bf16(const lsr_muon_group* groups, int ngroups, float momentum, int nesterov, int ns_steps,
                                 float a, float b, float c, float eps, void* const* updates, void* ws, size_t ws_bytes,
                                 lsr_stream_t stream) {
+  return lsr_muon_orthogonalize_phase_bf16(groups, ngroups, momentum, nesterov, ns_steps, a, b, c, eps, updates, 3, ws,
+                                           ws_bytes, stream);
+}
+
+int lsr_muon_orthogonalize_phase_bf16(const lsr_muon_group* groups, int ngroups, float momentum, int nesterov,
+                                      int ns_steps, float a, float b, float c, float eps, void* const* updates,
+                                      int phase, void* ws, size_t ws_bytes, lsr_stream_t stream) {
+  if (phase < 1 || phase > 3) return LSR_ERR_ARG;
   if (!valid_groups(groups, ngroups) || ns_steps < 0 || !updates) return LSR_ERR_ARG;
   for (int i = 0; i < ngroups; ++i) {
     if (groups[i].count > 65535) return LSR_ERR_SHAPE;
@@ -743,7 +759,7 @@ int lsr_muon_orthogonalize_bf16(const lsr_muon_group* groups, int ngroups, float
     gs[i].final_bs = (long long)gs[i].m * gs[i].n;
     gs[i].final_trans = 0;
   }
-  return muon_orthogonalize(groups, ngroups, gs, momentum, nesterov, ns_steps, a, b, c, eps, st);
+  return muon_orthogonalize(groups, ngroups, gs, momentum, nesterov, ns_steps, a, b, c, eps, st, phase);
 }
 
 int lsr_muon_apply_bf16(const lsr_muon_group* groups, int ngroups, const void* const* updates, float weight_decay,

@@ -113,6 +113,11 @@ SIGNATURES: dict[str, tuple] = {
         [ctypes.POINTER(MuonGroup), c_int, c_float, c_int, c_int, c_float, c_float, c_float, c_float,
          ctypes.POINTER(c_void_p), c_void_p, c_size_t, c_void_p],
     ),
+    "lsr_muon_orthogonalize_phase_bf16": (
+        c_int,
+        [ctypes.POINTER(MuonGroup), c_int, c_float, c_int, c_int, c_float, c_float, c_float, c_float,
+         ctypes.POINTER(c_void_p), c_int, c_void_p, c_size_t, c_void_p],
+    ),
     "lsr_muon_apply_bf16": (
         c_int,
         [ctypes.POINTER(MuonGroup), c_int, ctypes.POINTER(c_void_p), c_float, c_float, c_void_p],

@@ -151,6 +151,7 @@ class ShardGroup:
     gather_buf: torch.Tensor | None = None  # [world * per, m, n]
     flat_buf: torch.Tensor | None = None    # flat mode: parameters, rank-major [world * per, r, c]
     own_slice: torch.Tensor | None = None   # flat mode: this rank's slots of flat_buf
+    ws: torch.Tensor | None = None          # workspace kept between the two orthogonalize phases
 
 
 class ShardedMuon:
@@ -246,15 +247,23 @@ class ShardedMuon:
             for dst, src in zip(G.momentum, bufs):
                 dst.copy_(src)
 
-    def _orthogonalize(self, G: ShardGroup) -> None:
+    def _orthogonalize(self, G: ShardGroup, phase: int = 3) -> None:
+        """phase 3: momentum + Newton–Schulz; phase 1 / 2: the two halves, sharing G.ws."""
         items = [(G.params[j], G.params[j].grad, G.momentum[k], G.lr) for k, j in enumerate(G.owned)]
         if any(it[1] is None for it in items):
             raise RuntimeError("ShardedMuon: every owned parameter needs a gradient")
         if not items:
             return
         grouped = [(G.shape, G.lr, items)]
-        self.engine.orthogonalize(grouped, momentum=self.mu, nesterov=self.nesterov, ns_steps=self.ns_steps,
-                                  eps=self.eps, coef=(NS_A, NS_B, NS_C), out=[G.local_buf[:len(items)]])
+        kw = dict(momentum=self.mu, nesterov=self.nesterov, ns_steps=self.ns_steps, eps=self.eps,
+                  coef=(NS_A, NS_B, NS_C), out=[G.local_buf[:len(items)]])
+        if phase == 3:
+            self.engine.orthogonalize(grouped, **kw)
+            return
+        if G.ws is None:
+            G.ws = torch.empty(self.engine.workspace_bytes(grouped) + 256, dtype=torch.uint8,
+                               device=items[0][0].device)
+        self.engine.orthogonalize_phase(grouped, phase, G.ws, **kw)
 
     def _apply(self, G: ShardGroup) -> None:
         order = gathered_order(len(G.params), self.world)
@@ -298,9 +307,15 @@ class ShardedMuon:
             return
         compute = torch.cuda.current_stream()
         comm = self.comm_stream
+        # every group's memory-bound prologue (momentum, orientation, norm) first,
+        # while no exchange competes for HBM and SMs
+        phased = hasattr(self.engine, "orthogonalize_phase")
+        if phased:
+            for gi in self.flat_order:
+                self._orthogonalize(self.groups[gi], phase=1)
         for gi in self.flat_order:
             G = self.groups[gi]
-            self._orthogonalize(G)
+            self._orthogonalize(G, phase=2 if phased else 3)
             self._apply_own(G)
             ev = torch.cuda.Event()
             ev.record(compute)

@@ -188,6 +188,28 @@ class MuonStepEngine:
         del keep
         return out
 
+    def workspace_bytes(self, grouped) -> int:
+        arr, keep = self.make_groups(grouped)
+        n = _lib.load().lsr_muon_workspace_bytes(arr, len(arr))
+        del keep
+        return int(n)
+
+    def orthogonalize_phase(self, grouped, phase, workspace, *, momentum, nesterov, ns_steps, eps,
+                            coef=(NS_A, NS_B, NS_C), out):
+        """orthogonalize() in two calls sharing `workspace` (uint8 CUDA tensor of at least
+        workspace_bytes(grouped)): phase 1 = momentum / orientation / normalisation, phase 2 =
+        Newton–Schulz into ``out``."""
+        dev = grouped[0][2][0][0].device
+        arr, keep = self.make_groups(grouped)
+        ptrs = (ctypes.c_void_p * len(out))(*[o.data_ptr() for o in out])
+        with torch.cuda.device(dev):
+            rc = _lib.load().lsr_muon_orthogonalize_phase_bf16(
+                arr, len(arr), float(momentum), int(bool(nesterov)), int(ns_steps), float(coef[0]), float(coef[1]),
+                float(coef[2]), float(eps), ptrs, int(phase), workspace.data_ptr(), workspace.numel(),
+                _lib.stream_handle(dev))
+        _lib.check(rc, "lsr_muon_orthogonalize_phase_bf16")
+        del keep
+
     def apply(self, grouped, updates, *, weight_decay, base_lr):
         """p *= 1 - base_lr*wd ; p -= lr_adj * update, for every group (updates oriented [count, m, n])."""
         if not grouped:

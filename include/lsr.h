@@ -145,6 +145,17 @@ LSR_API int lsr_muon_orthogonalize_bf16(const lsr_muon_group* groups, int ngroup
                                 int ns_steps, float a, float b, float c, float eps, void* const* updates,
                                 void* ws, size_t ws_bytes, lsr_stream_t stream);
 
+/* The same in two calls that share `ws` (same groups, same ws pointer):
+ * phase 1 runs the momentum update, orientation and Frobenius normalisation
+ * into the workspace; phase 2 the Newton–Schulz iterations from there into
+ * updates[g]; phase 3 both (= lsr_muon_orthogonalize_bf16). Lets a sharded
+ * step run every group's memory-bound prologue before the parameter exchange
+ * of the first group starts. */
+LSR_API int lsr_muon_orthogonalize_phase_bf16(const lsr_muon_group* groups, int ngroups, float momentum,
+                                              int nesterov, int ns_steps, float a, float b, float c, float eps,
+                                              void* const* updates, int phase, void* ws, size_t ws_bytes,
+                                              lsr_stream_t stream);
+
 /* Sharded step, part 2: apply oriented updates (e.g. after an all-gather) to
  * the parameters of `groups` (grad/mom pointers are not read). */
 LSR_API int lsr_muon_apply_bf16(const lsr_muon_group* groups, int ngroups, const void* const* updates,

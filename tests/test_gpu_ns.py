@@ -216,3 +216,33 @@ def test_cpu_tensor_raises():
     import lsr
     with pytest.raises(ValueError):
         lsr.zeropower_serial(torch.zeros(8, 8, dtype=torch.bfloat16), 5, 1e-7)
+
+
+def test_orthogonalize_in_two_phases_is_identical():
+    """lsr_muon_orthogonalize_phase_bf16: phase 1 then phase 2 over one workspace equals the
+    one-call orthogonalize bit for bit (the sharded step runs every prologue first)."""
+    from lsr.muon import MuonStepEngine, adjusted_muon_lr
+    shapes = [(256, 768), (768, 256), (384, 384)]
+    g = torch.Generator().manual_seed(12)
+    P = [(torch.randn(*s, generator=g) * 0.02).bfloat16().cuda() for s in shapes]
+    Gr = [(torch.randn(*s, generator=g) * 0.01).bfloat16().cuda() for s in shapes]
+    M0 = [(torch.randn(*s, generator=g) * 0.01).bfloat16().cuda() for s in shapes]
+    eng = MuonStepEngine()
+    outs = []
+    for phased in (False, True):
+        M = [m.clone() for m in M0]
+        grouped = eng.group_items([(p, gr, m, adjusted_muon_lr(0.02, p.shape, "original"))
+                                   for p, gr, m in zip(P, Gr, M)])
+        out = [torch.empty(len(its), min(s), max(s), dtype=torch.bfloat16, device="cuda") for s, _, its in grouped]
+        kw = dict(momentum=0.95, nesterov=True, ns_steps=5, eps=1e-7, out=out)
+        if phased:
+            ws = torch.empty(eng.workspace_bytes(grouped) + 256, dtype=torch.uint8, device="cuda")
+            eng.orthogonalize_phase(grouped, 1, ws, **kw)
+            eng.orthogonalize_phase(grouped, 2, ws, **kw)
+        else:
+            eng.orthogonalize(grouped, **kw)
+        outs.append((out, M))
+    for a, b in zip(outs[0][0], outs[1][0]):
+        assert torch.equal(a, b)
+    for a, b in zip(outs[0][1], outs[1][1]):
+        assert torch.equal(a, b)
