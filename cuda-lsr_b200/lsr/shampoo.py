@@ -23,6 +23,9 @@ config objects and runs the preconditioner math in liblsr:
   the inverse roots / eigenbases are recomputed from L, R with an fp32
   eigendecomposition (``torch.linalg.eigh``, the periodic step; before the
   first one Shampoo uses the grafting direction and SOAP the identity basis);
+  ``root_inverse_method="coupled_newton"`` computes Shampoo's inverse 4th
+  roots with the batched coupled Newton kernel instead (``lsr.newton``, the
+  recurrence of shampoo.py:277-542, all blocks of one shape in one call);
 * with ``DDPDistributedConfig`` and an initialised process group the blocks
   are owned by ranks (greedy by flops, ZeRO-1: state only for owned blocks),
   directions are all-gathered in ``communication_dtype`` and every rank
@@ -140,7 +143,7 @@ class DistributedShampoo(torch.optim.Optimizer):
                  max_preconditioner_dim=1024, precondition_frequency=1, start_preconditioning_step=-1,
                  weight_decay_type=WeightDecayType.DECOUPLED, distributed_config: Optional[DDPDistributedConfig] = None,
                  grafting_config: Optional[AdamPreconditionerConfig] = None, preconditioner_config=None,
-                 eager_nan_check: bool = False, **unused):
+                 eager_nan_check: bool = False, root_inverse_method: str = "eigh", **unused):
         if weight_decay_type != WeightDecayType.DECOUPLED:
             raise ValueError("only WeightDecayType.DECOUPLED is supported")
         if max_preconditioner_dim % 8:
@@ -148,6 +151,9 @@ class DistributedShampoo(torch.optim.Optimizer):
         defaults = dict(lr=lr, betas=betas, epsilon=epsilon, weight_decay=weight_decay)
         super().__init__(params, defaults)
         self.soap = isinstance(preconditioner_config, EigenvalueCorrectedShampooConfig)
+        if root_inverse_method not in ("eigh", "coupled_newton"):
+            raise ValueError(f"root_inverse_method must be 'eigh' or 'coupled_newton', got {root_inverse_method!r}")
+        self.root_inverse_method = root_inverse_method
         self.grafting = grafting_config or AdamPreconditionerConfig(beta2=betas[1], epsilon=1e-8)
         self.max_dim = max_preconditioner_dim
         self.freq = max(1, precondition_frequency)
@@ -199,6 +205,10 @@ class DistributedShampoo(torch.optim.Optimizer):
             _, QL = torch.linalg.eigh(grp.L + eps * eye_r)
             _, QR = torch.linalg.eigh(grp.R + eps * eye_c)
             grp.QL, grp.QR = QL.bfloat16().contiguous(), QR.bfloat16().contiguous()
+        elif self.root_inverse_method == "coupled_newton":
+            from .newton import batched_coupled_newton
+            grp.QL = batched_coupled_newton(grp.L, 4, epsilon=eps)[0].bfloat16().contiguous()
+            grp.QR = batched_coupled_newton(grp.R, 4, epsilon=eps)[0].bfloat16().contiguous()
         else:
             def root(S, I):
                 w, V = torch.linalg.eigh(S + eps * I)

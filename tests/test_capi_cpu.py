@@ -112,3 +112,33 @@ def test_shampoo_block_partition_and_owners():
         loads = [sum(cc for cc, o in zip(costs, own) if o == k) for k in range(world)]
         assert set(own) <= set(range(world))
         assert max(loads) <= sum(costs) / world + max(costs)
+
+
+def test_coupled_newton_host_checks_without_gpu():
+    """Coupled Newton: workspace sizing and argument checks need no GPU; CPU tensors raise."""
+    import lsr
+    from lsr import _lib
+    lib = _lib.load()
+    assert lib.lsr_coupled_newton_workspace_bytes(2, 6) == 0          # n not a multiple of 4
+    nb = lib.lsr_coupled_newton_workspace_bytes(2, 8)
+    assert nb >= 14 * 2 * 8 * 8 * 4
+    # root 3 / negative iteration bound rejected before any device work; empty batch is a no-op
+    assert lib.lsr_coupled_newton_f32(None, None, None, None, None, 1, 8, 3, 0.0, 1e-6, 100, 4, 0, None, 0,
+                                      None) == -1
+    assert lib.lsr_coupled_newton_f32(None, None, None, None, None, 1, 8, 2, 0.0, 1e-6, -1, 4, 0, None, 0,
+                                      None) == -1
+    assert lib.lsr_coupled_newton_f32(None, None, None, None, None, 0, 8, 2, 0.0, 1e-6, 100, 4, 0, None, 0,
+                                      None) == 0
+    with pytest.raises(ValueError):
+        lsr.batched_coupled_newton(torch.eye(8).expand(2, 8, 8).contiguous(), 2)
+
+
+def test_peer_push_argument_checks_without_gpu():
+    import ctypes
+    from lsr import _lib
+    lib = _lib.load()
+    d = (ctypes.c_longlong * 1)(16)
+    assert lib.lsr_peer_push(None, 2, d, 16, 0, None) == -1   # more peers than supported
+    assert lib.lsr_peer_push(None, 3, d, 1, 0, None) == -1    # odd byte count
+    assert lib.lsr_peer_push(None, 0, d, 1, 0, None) == 0     # nothing to do
+    assert lib.lsr_ipc_open(None, None) == -1

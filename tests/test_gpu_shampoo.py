@@ -97,3 +97,28 @@ def test_distributed_shampoo_soap_plumbing():
     n_blocks = sum(len(param_blocks(s, 512)) for s in shapes)
     assert sum(len(grp.refs) for _, grp, _ in opt._groups) == n_blocks
     assert torch.isfinite(bias).all() and bias.abs().sum() > 0
+
+
+def test_shampoo_roots_by_coupled_newton_match_eigh():
+    """root_inverse_method="coupled_newton": the inverse 4th roots of L + eps I, R + eps I from the
+    batched coupled Newton kernel agree with the eigendecomposition path (bf16-stored roots)."""
+    from lsr.shampoo import DistributedShampoo
+    g = torch.Generator().manual_seed(8)
+    shapes = [(128, 384), (256, 256)]
+    P0 = [(torch.randn(*s, generator=g) * 0.02).bfloat16() for s in shapes]
+    grads = [(torch.randn(*s, generator=g) * 0.01).bfloat16() for s in shapes]
+    roots = {}
+    for method in ("eigh", "coupled_newton"):
+        params = [torch.nn.Parameter(p.clone().cuda()) for p in P0]
+        opt = DistributedShampoo(params, lr=0.01, betas=(0.9, 0.95), epsilon=1e-3, weight_decay=0.0,
+                                 max_preconditioner_dim=512, precondition_frequency=1, start_preconditioning_step=1,
+                                 root_inverse_method=method)
+        for p, gr in zip(params, grads):
+            p.grad = gr.cuda()
+        opt.step()
+        roots[method] = [(grp.QL.float().cpu(), grp.QR.float().cpu()) for _, grp, _ in opt._groups]
+    for (le, re), (ln, rn) in zip(roots["eigh"], roots["coupled_newton"]):
+        assert rel_fro(ln.numpy(), le.numpy()) < 1e-2
+        assert rel_fro(rn.numpy(), re.numpy()) < 1e-2
+    with pytest.raises(ValueError):
+        DistributedShampoo([torch.nn.Parameter(P0[0].cuda())], root_inverse_method="qr")
