@@ -374,23 +374,37 @@ __device__ __forceinline__ void epilogue_chunk_staged(const GemmParams& p, int g
                                                       uint8_t* tbuf) {
   using T = EpiT<EPI>;
   if constexpr (EPI == EPI_SOAP_ADAM) {
-    // Stage the fp32 accumulator rows, then work row-contiguously: 8 lanes per
-    // row, 16-byte vectors, so m / v / u move in coalesced segments.
+    // Work row-contiguously: 8 lanes per row, 16-byte vectors, so m / v / u move
+    // in coalesced segments. All eight rows' m and v loads of this lane are
+    // issued first (256 B in flight per lane), then the accumulator rows are
+    // staged, so the loads' latency overlaps the staging.
+    const int jv = lane & 7;
+    float4 mr[8], vr[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int gr = row0 + (lane >> 3) + 4 * i, gc = col0 + 4 * jv;
+      mr[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      vr[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (gr < G.M && gc < G.N) {
+        const long long idx = (long long)b * G.out_bs + (long long)gr * G.ldo + gc;
+        mr[i] = *reinterpret_cast<const float4*>(G.st_m + idx);
+        vr[i] = *reinterpret_cast<const float4*>(G.st_v + idx);
+      }
+    }
     __syncwarp();  // the previous chunk's reads of dbuf are done
 #pragma unroll
     for (int j = 0; j < 8; ++j)
       *reinterpret_cast<uint4*>(dbuf + stg_off<128>(lane, j)) = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
     __syncwarp();
-    const int jv = lane & 7;
-#pragma unroll 2
+#pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int rr = (lane >> 3) + 4 * i;
       const int gr = row0 + rr, gc = col0 + 4 * jv;
       if (gr >= G.M || gc >= G.N) continue;
       const float4 g4 = *reinterpret_cast<const float4*>(dbuf + stg_off<128>(rr, jv));
       const long long idx = (long long)b * G.out_bs + (long long)gr * G.ldo + gc;
-      float4 m4 = *reinterpret_cast<const float4*>(G.st_m + idx);
-      float4 v4 = *reinterpret_cast<const float4*>(G.st_v + idx);
+      float4 m4 = mr[i];
+      float4 v4 = vr[i];
       const float gg[4] = {g4.x, g4.y, g4.z, g4.w};
       float mm[4] = {m4.x, m4.y, m4.z, m4.w}, vv[4] = {v4.x, v4.y, v4.z, v4.w}, uu[4];
 #pragma unroll

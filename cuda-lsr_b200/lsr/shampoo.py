@@ -124,8 +124,11 @@ class _BlockGroup:
         self.stack = torch.empty(n, r, c, dtype=torch.bfloat16, device=device)
         self.U = torch.empty(n, r, c, dtype=torch.float32, device=device)
         self._ptr_key = None
+        self._grad_key = None
 
     def pointers(self):
+        """Device arrays of the blocks' parameter and gradient addresses and row strides,
+        rebuilt (a small host-to-device copy) only when a tensor has moved."""
         key = tuple(p.data_ptr() for p, _, _ in self.refs)
         if key != self._ptr_key:
             dev = self.stack.device
@@ -133,9 +136,12 @@ class _BlockGroup:
                 [p.data_ptr() + 2 * (r0 * p.shape[1] + c0) for p, r0, c0 in self.refs], dtype=torch.int64).to(dev)
             self.lds = torch.tensor([p.shape[1] for p, _, _ in self.refs], dtype=torch.int32).to(dev)
             self._ptr_key = key
-        grad_ptrs = torch.tensor([p.grad.data_ptr() + 2 * (r0 * p.shape[1] + c0) for p, r0, c0 in self.refs],
-                                 dtype=torch.int64).to(self.stack.device)
-        return self.data_ptrs, self.lds, grad_ptrs
+        gkey = tuple(p.grad.data_ptr() for p, _, _ in self.refs)
+        if gkey != self._grad_key:
+            self.grad_ptrs = torch.tensor([p.grad.data_ptr() + 2 * (r0 * p.shape[1] + c0) for p, r0, c0 in self.refs],
+                                          dtype=torch.int64).to(self.stack.device)
+            self._grad_key = gkey
+        return self.data_ptrs, self.lds, self.grad_ptrs
 
 
 class DistributedShampoo(torch.optim.Optimizer):
