@@ -127,6 +127,20 @@ __global__ void __launch_bounds__(EW_THREADS) orient_kernel(MatRef src, MatRef m
                    (!MOMENTUM || aligned16(buf));
   if (vec) {
     uint32_t* tile = reinterpret_cast<uint32_t*>(smem);
+    // both rows' gradient and momentum vectors are loaded before anything is
+    // stored (the stores could alias later loads, so the compiler would not
+    // hoist them): twice the bytes in flight per thread
+    uint4 gv[2], bv[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int r = r0 + (tid >> 3) + 32 * k, c = c0 + 8 * (tid & 7);
+      gv[k] = bv[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (r < R && c < C) {
+        const long long idx = (long long)r * C + c;
+        gv[k] = *reinterpret_cast<const uint4*>(g + idx);
+        if constexpr (MOMENTUM) bv[k] = *reinterpret_cast<const uint4*>(buf + idx);
+      }
+    }
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const int i = (tid >> 3) + 32 * k;
@@ -136,8 +150,8 @@ __global__ void __launch_bounds__(EW_THREADS) orient_kernel(MatRef src, MatRef m
       if (r < R && c < C) {
         const long long idx = (long long)r * C + c;
         float gf[8], bf[8];
-        unpack8(*reinterpret_cast<const uint4*>(g + idx), gf);
-        if constexpr (MOMENTUM) unpack8(*reinterpret_cast<const uint4*>(buf + idx), bf);
+        unpack8(gv[k], gf);
+        if constexpr (MOMENTUM) unpack8(bv[k], bf);
         momentum8<MOMENTUM>(gf, bf, u, mu, nesterov);
         if constexpr (MOMENTUM) *reinterpret_cast<uint4*>(buf + idx) = pack8(bf);
 #pragma unroll
