@@ -288,7 +288,10 @@ class DistributedShampoo(torch.optim.Optimizer):
         _lib.check(lib.lsr_shampoo_direction_bf16(Gfb.data_ptr(), None, None, grp.QL.data_ptr(), grp.QR.data_ptr(),
                                                   grp.U.data_ptr(), n, r, c, 0.0, 0, ws.data_ptr(), nb,
                                                   _lib.stream_handle(Gfb.device)), "lsr_shampoo_direction_bf16")
-        scale = adam.flatten(1).norm(dim=1) / grp.U.flatten(1).norm(dim=1).clamp_min(1e-30)
+        # per-block norms accumulated in fp64: torch picks its reduction order from the stack's shape,
+        # and this keeps a block's scale independent of which blocks share its stack
+        scale = (adam.double().flatten(1).norm(dim=1) /
+                 grp.U.double().flatten(1).norm(dim=1).clamp_min(1e-30)).float()
         grp.U.mul_(scale[:, None, None])
 
     def _exchange_and_apply(self, shape, grp, lst, lr, wd):
