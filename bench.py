@@ -14,9 +14,11 @@ parameters N(0, 0.02^2), bf16, seeded (seed 4) on the device.
 N > 1 is launched with torch.distributed.run: the matrices of each shape group
 are sharded round-robin over the ranks (ZeRO-1), the orthogonalised updates are
 all-gathered with NCCL and applied on every rank (total work fixed: strong
-scaling). ``--impl reference`` times the CPU restatement of the reference path
-(the oracle; the reference itself is Python/torch) on the host cores, on a
-bounded sample extrapolated to the full step.
+scaling). ``--impl reference`` times the reference's own Muon step
+(muon_lm_ddp.MuonAdamW.muon_step, torch on the host cores, the module staged
+unmodified in oracle/_ref/ by oracle/stage_reference.py; the numpy
+restatement in oracle/muon.py when it is not staged) on a bounded sample, one
+of the 48 layers per step, extrapolated to the full step.
 
 Rank 0 prints one JSON line.
 """
@@ -164,25 +166,77 @@ def cpu_layer_step_ms(seed: int = 4) -> float:
     return (time.perf_counter() - t0) * 1e3
 
 
+def load_reference_module(name: str = "muon_lm_ddp"):
+    """The reference's own module `name` as staged in oracle/_ref/ (None when not staged)."""
+    from oracle import stage_reference
+    path = stage_reference.staged_module_path(name + ".py")
+    if path is None:
+        return None
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+class ReferenceLayerStep:
+    """One layer's Muon step (c_attn 1600x4800, attn.c_proj 1600x1600, mlp.c_fc 1600x6400,
+    mlp.c_proj 6400x1600) through the reference's own MuonAdamW.muon_step on CPU tensors,
+    with the benchmark's hyper-parameters (muon_lm_ddp.py:433-696, batched mode, chunks of 8)."""
+
+    def __init__(self, mod, seed: int = 4):
+        g = torch.Generator().manual_seed(seed)
+        self.params = [torch.nn.Parameter((torch.randn(*s, generator=g) * 0.02).bfloat16()) for s in LAYER_SHAPES]
+        named = [(f"transformer.h.0.w{i}", p) for i, p in enumerate(self.params)]
+        self.opt = mod.MuonAdamW(named, "batched", LR, MU, WD, True, NS_STEPS, EPS, "original", 8, 3e-4,
+                                 (0.9, 0.95), 0.0, 0)
+        for p in self.params:
+            self.opt.momentum[p].copy_((torch.randn(*p.shape, generator=g) * 0.01).bfloat16())
+            p.grad = (torch.randn(*p.shape, generator=g) * 0.01).bfloat16()
+
+    def __call__(self) -> float:
+        t0 = time.perf_counter()
+        self.opt.muon_step()
+        return (time.perf_counter() - t0) * 1e3
+
+
+def cpu_baseline_sampler():
+    """(callable returning one layer's step ms, kind, description) for the CPU baseline: the reference's
+    own torch code when staged in oracle/_ref/, else the numpy restatement of it."""
+    mod = load_reference_module()
+    if mod is not None:
+        torch.set_num_threads(os.cpu_count() or 1)
+        step = ReferenceLayerStep(mod)
+        return step, "reference", (f"muon_lm_ddp.MuonAdamW.muon_step (the reference module, unmodified, "
+                                   f"torch on {torch.get_num_threads()} CPU threads) on 1 of 48 layers "
+                                   f"(4 matrices 1600x4800, 1600x1600, 1600x6400, 6400x1600), extrapolated x48")
+    return cpu_layer_step_ms, "port", ("1 of 48 layers (4 matrices 1600x4800, 1600x1600, 1600x6400, 6400x1600), "
+                                       "full Muon step (momentum, 5 NS steps, apply) through the numpy "
+                                       "restatement of the reference, extrapolated x48")
+
+
 def run_reference_arm(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    cores = os.cpu_count() or 1
+    fn, kind, desc = cpu_baseline_sampler()
+    cores = torch.get_num_threads() if kind == "reference" else (os.cpu_count() or 1)
     for _ in range(args.warmup):
-        cpu_layer_step_ms()
-    samples = [cpu_layer_step_ms() for _ in range(args.steps)]
+        fn()
+    samples = [fn() for _ in range(args.steps)]
     layer_ms = statistics.median(samples)
     value = layer_ms * N_LAYERS
-    sample = (f"1 of 48 layers (4 matrices 1600x4800, 1600x1600, 1600x6400, 6400x1600), full Muon step "
-              f"(momentum, 5 NS steps, apply) through the numpy restatement, x48; median of {args.steps}")
+    sample = f"{desc}; median of {args.steps} one-layer samples"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "ms", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 3), "higher_is_better": False,
         "scaling": "strong", "vs_baseline": round(value / BASELINE_MS, 4), "dtype": "bf16",
         "data": "synthetic (seeded N(0,0.01^2) grads/momentum, N(0,0.02^2) params)",
         "config": {"workload": WORKLOAD, "parallelism": "host cores", "l2": "n/a (CPU)"},
-        "cpu_baseline": {"value": round(value, 3), "unit": "ms", "cores": cores, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": round(value, 3), "unit": "ms", "cores": cores, "kind": kind, "sample": sample,
+                         "extrapolated": {"from": "1 layer of 48", "factor": N_LAYERS,
+                                          "layer_ms_median": round(layer_ms, 3),
+                                          "timed_wall_s": round(sum(samples) / 1e3, 2)}},
         "e2e": {"value": round(value, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -324,9 +378,12 @@ def run_lsr(args) -> None:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        layer_ms = statistics.median([cpu_layer_step_ms() for _ in range(2)])
-        cpu = {"value": round(layer_ms * N_LAYERS, 1), "unit": "ms", "cores": os.cpu_count() or 1, "kind": "port",
-               "sample": "1 of 48 layers (4 matrices), full Muon step via the numpy restatement, x48; median of 2"}
+        fn, kind, desc = cpu_baseline_sampler()
+        fn()  # warm-up
+        layer_ms = statistics.median([fn() for _ in range(3)])
+        cores = torch.get_num_threads() if kind == "reference" else (os.cpu_count() or 1)
+        cpu = {"value": round(layer_ms * N_LAYERS, 1), "unit": "ms", "cores": cores, "kind": kind,
+               "sample": f"{desc}; median of 3"}
 
     if rank == 0:
         line = {
@@ -342,11 +399,15 @@ def run_lsr(args) -> None:
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    e2e_invalid = e2e is not None and not e2e.get("valid", True)
     if world > 1:
         import torch.distributed as dist
         opt.close()
         dist.barrier()
         dist.destroy_process_group()
+    if e2e_invalid:
+        # a wrong host copy must not pass as a timing: the run fails
+        raise SystemExit("e2e: the downloaded parameters differ from the device parameters")
 
 
 def run_e2e(args, params, grads, step, world, opt):
@@ -429,9 +490,9 @@ def run_e2e(args, params, grads, step, world, opt):
     barrier(world)
     ms = max_over_ranks(a.elapsed_time(b) / n, world)
     # the host copy is the step's result: check it against the device parameters
-    matches = all(torch.equal(h, p.data.cpu()) for h, p in list(zip(host_p, params))[:2])
-    return {"value": round(ms, 3), "unit": "ms", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-            "host_copy_matches_device": bool(matches),
+    matches = all(torch.equal(h, p.data.cpu()) for h, p in zip(host_p, params))
+    return {"value": round(ms, 3) if matches else None, "unit": "ms", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "host_copy_matches_device": bool(matches), "valid": bool(matches),
             "steps": n, "path": "lsr.MuonAdamW.muon_step" if world == 1 else "lsr.dist.ShardedMuon.step",
             "pipelining": "double-buffered device gradients (upload of step i+1 during step i) and a device "
                           "snapshot of the parameters (download of step i during step i+1); two copy streams"}
@@ -454,14 +515,16 @@ def load_traffic(kind: str):
 # ---------------------------------------------------------------------------
 
 def _time_gpu(fn, warmup, iters, flush_bytes=256 << 20):
-    """Mean ms of fn() over `iters` runs, L2 flushed (a buffer larger than L2 is written) before each."""
-    flush = torch.empty(flush_bytes, dtype=torch.uint8, device="cuda")
+    """Mean ms of fn() over `iters` runs, L2 flushed (a buffer larger than L2 is written) before each
+    unless flush_bytes is 0."""
+    flush = torch.empty(flush_bytes, dtype=torch.uint8, device="cuda") if flush_bytes else None
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     tot = 0.0
     for _ in range(iters):
-        flush.zero_()
+        if flush is not None:
+            flush.zero_()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         fn()
@@ -602,6 +665,41 @@ def run_workload(args) -> None:
                                       f"{sum(len(grp.refs) for _, grp, _ in opt._groups)} blocks at 1024, 1 GPU",
                           "value": ms, "unit": "ms", "algorithmic_tflop": fl / 1e12, "tflops": fl / ms / 1e9,
                           "frac_of_sustained": fl / ms / 1e9 / peaks["bf16_tflops_sustained"]})
+    elif w == "kron64x8":
+        # The reference's own Kronecker-sum sweep (hft_fused.py:856-862): x [M, 64, 8], S terms
+        # A_s [64,64] / sqrt(64), B_s [8,8] / sqrt(8), at = A^T prepacked, fp32 (TF32 off). Its
+        # kron_sum_64x8_kernel (built from the staged hft_fused.py by its own load_inline) and
+        # lsr.kron.kron_sum_out run on the same inputs and GPU, timed the same way (no L2 flush, as
+        # the reference's median_ms); results are compared against the fp64 product.
+        ref = load_reference_module("hft_fused")
+        torch.backends.cuda.matmul.allow_tf32 = False
+        for M in (256, 1024, 4096, 16384):
+            for S in (1, 2, 4, 8):
+                gk = torch.Generator(device=dev).manual_seed(17 + 1000 * M + S)
+                X = torch.randn(M, 64, 8, device=dev, generator=gk)
+                A = torch.randn(S, 64, 64, device=dev, generator=gk) / 8.0
+                B = torch.randn(S, 8, 8, device=dev, generator=gk) / math.sqrt(8)
+                AT = A.transpose(1, 2).contiguous()
+                Y = torch.empty_like(X)
+                Yd = torch.einsum("sik,mkl,sjl->mij", A.double(), X.double(), B.double())
+
+                def ours():
+                    K.kron_sum_out(X, AT, B, Y)
+                ms = _time_gpu(ours, args.warmup, max(args.steps, 20), flush_bytes=0)
+                err = ((Y.double() - Yd).norm() / Yd.norm()).item()
+                line = {"workload": f"kron64x8: x [{M},64,8], S={S}, fp32", "value": ms, "unit": "ms",
+                        "rel_err_vs_fp64": err}
+                if ref is not None:
+                    Yr = torch.empty_like(X)
+
+                    def theirs():
+                        ref.ext.kron_sum_out(X, AT, B, Yr)
+                    ms_ref = _time_gpu(theirs, args.warmup, max(args.steps, 20), flush_bytes=0)
+                    line.update({"reference_kernel_ms": ms_ref, "speedup_vs_reference_kernel": ms_ref / ms,
+                                 "reference_rel_err_vs_fp64": ((Yr.double() - Yd).norm() / Yd.norm()).item()})
+                else:
+                    line["reference_kernel_ms"] = None
+                lines.append(line)
     elif w == "f1":
         # Batched coupled Newton inverse roots on the reference's full bucket list
         # (shampoo.py:812-840: (n, root, B), seeds 17 + 100 j, tolerance 1e-6,
@@ -693,7 +791,8 @@ def main(argv=None) -> int:
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="nccl",
                     help="N>1: parameter exchange (peer-memory push or NCCL all-gather)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["muon", "cfg1", "cfg2", "cfg3", "cfg5", "f1", "muon_torch"], default="muon",
+    ap.add_argument("--workload", choices=["muon", "cfg1", "cfg2", "cfg3", "cfg5", "f1", "muon_torch", "kron64x8"],
+                    default="muon",
                     help="muon = the headline GPT-2-XL Muon step (default); cfgN = per-row workloads")
     args = ap.parse_args(argv)
     if args.workload != "muon" and args.impl == "lsr":

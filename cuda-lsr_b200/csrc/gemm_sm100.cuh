@@ -48,7 +48,8 @@ enum : int {
   EPI_SPLIT_TF32 = 7,    // out = tf32(acc), out2 = acc - tf32(acc)        (hi/lo fp32 pair)
   EPI_SOAP_ADAM = 8,     // Adam in the rotated basis on g = acc, fp32 moments st_m / st_v:
                          //   m = b1 m + (1-b1) g ; v = b2 v + (1-b2) g^2
-                         //   u = (m * c1) / (sqrt(v * c2) + eps) -> out (bf16)
+                         //   u = (m * c1) / (sqrt(v * c2) + eps) -> out = bf16(u),
+                         //   out2 = bf16(u - bf16(u)) when out2 is set (hi/lo bf16 pair)
 };
 
 // Round an fp32 value to tf32 (10 explicit mantissa bits, nearest, ties away
@@ -152,6 +153,7 @@ enum : int {
   ST_TIMEOUT_EPILOGUE = 104,
   ST_TIMEOUT_TEARDOWN = 105,
   ST_TIMEOUT_TILE_QUEUE = 106,
+  ST_TIMEOUT_PROLOGUE = 107,  // Muon prologue: a matrix's norm was not published in time
 };
 
 // ---------------------------------------------------------------------------
@@ -217,6 +219,7 @@ __device__ __forceinline__ void epilogue_chunk(const GroupDesc& G, int b, int ro
     float* pm = G.st_m + rowoff;
     float* pv = G.st_v + rowoff;
     __nv_bfloat16* pu = reinterpret_cast<__nv_bfloat16*>(G.out) + rowoff;
+    __nv_bfloat16* pl = G.out2 ? reinterpret_cast<__nv_bfloat16*>(G.out2) + rowoff : nullptr;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       if (j >= ncols) continue;
@@ -225,7 +228,10 @@ __device__ __forceinline__ void epilogue_chunk(const GroupDesc& G, int b, int ro
       const float vv = fmaf(G.b2, pv[j], (1.f - G.b2) * g * g);
       pm[j] = mm;
       pv[j] = vv;
-      pu[j] = __float2bfloat16_rn((mm * G.c1) / (sqrtf(vv * G.c2) + G.eps));
+      const float u = (mm * G.c1) / (sqrtf(vv * G.c2) + G.eps);
+      const __nv_bfloat16 h = __float2bfloat16_rn(u);
+      pu[j] = h;
+      if (pl) pl[j] = __float2bfloat16_rn(u - __bfloat162float(h));
     }
     return;
   } else if constexpr (EPI == EPI_SPLIT_BF16X2 || EPI == EPI_SPLIT_TF32) {
@@ -420,6 +426,15 @@ __device__ __forceinline__ void epilogue_chunk_staged(const GemmParams& p, int g
       h[0] = __floats2bfloat162_rn(uu[0], uu[1]);
       h[1] = __floats2bfloat162_rn(uu[2], uu[3]);
       *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(G.out) + idx) = u2;
+      if (G.out2) {
+        // lo part of the pair: what bf16 rounding of u dropped
+        const float2 h0 = __bfloat1622float2(h[0]), h1 = __bfloat1622float2(h[1]);
+        uint2 l2;
+        __nv_bfloat162* l = reinterpret_cast<__nv_bfloat162*>(&l2);
+        l[0] = __floats2bfloat162_rn(uu[0] - h0.x, uu[1] - h0.y);
+        l[1] = __floats2bfloat162_rn(uu[2] - h1.x, uu[3] - h1.y);
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(G.out2) + idx) = l2;
+      }
     }
     return;
   }

@@ -86,6 +86,39 @@ bool kron_dims_ok(int batch, int m, int n, int nterms) {
   return batch >= 0 && batch <= 65535 && m > 0 && n > 0 && nterms > 0 && nterms <= 65535;
 }
 
+// Small factors (m n <= 1024, m n % 4 == 0): the fp32 apply forms the dense
+// operator W = sum_s A_s (x) B_s once ((m n)^2 entries, at most 4 MB) and runs
+// Y_flat = X_flat W^T as ONE tensor-core GEMM over every right-hand side
+// (rows = batch, K = N = m n), instead of 2 S chained GEMMs of m x n tiles that
+// would fill a fraction of a 128 x 256 tile each. This is the shape of
+// hft_fused.py's own kron_sum_64x8_kernel workload (x [M, 64, 8], S terms).
+constexpr int kDenseMaxMN = 1024;
+bool kron_use_dense(int m, int n) {
+  const long long mn = (long long)m * n;
+  return mn <= kDenseMaxMN && mn % 4 == 0;
+}
+
+// W[(i n + j)][(k n + l)] = sum_s A_s[i][k] B_s[j][l]  (A_s[i][k] = at[s][k][i] when a_trans),
+// written as a tf32 hi / lo pair.
+__global__ void __launch_bounds__(SPLIT_THREADS) kron_dense_w_kernel(const float* __restrict__ A, int a_trans,
+                                                                     const float* __restrict__ B, int m, int n, int S,
+                                                                     float* __restrict__ Wh, float* __restrict__ Wl) {
+  const int mn = m * n;
+  const long long total = (long long)mn * mn;
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(e / mn), col = (int)(e % mn);
+    const int i = row / n, j = row % n, k = col / n, l = col % n;
+    float acc = 0.f;
+    for (int s = 0; s < S; ++s) {
+      const float a = a_trans ? A[((long long)s * m + k) * m + i] : A[((long long)s * m + i) * m + k];
+      acc = fmaf(a, B[((long long)s * n + j) * n + l], acc);
+    }
+    const float h = tf32_hi(acc);
+    Wh[e] = h;
+    Wl[e] = acc - h;
+  }
+}
+
 // Operand helpers (all matrices row-major).
 //   mat(base, rows, cols, batch, mn, f32): `batch` matrices rows x cols, ld = cols.
 Operand mat(const void* base, int rows, int cols, int batch, int mn, int f32) {
@@ -199,6 +232,10 @@ size_t lsr_kron_apply_workspace_bytes(int batch, int m, int n, int nterms, int f
   if (!kron_dims_ok(batch, m, n, nterms)) return 0;
   const size_t mn = (size_t)batch * m * n;
   if (!f32) return 2 * a256(mn * 2) + 256;  // bf16 hi/lo intermediate
+  if (kron_use_dense(m, n)) {
+    const size_t w = (size_t)m * n * m * n * 4;
+    return 2 * a256(w) + 2 * a256(mn * 4) + 256;  // W hi/lo, X hi/lo
+  }
   // fp32: hi/lo of A (K-major), B, X (one orientation) and of the fp32 intermediate
   return 2 * (a256((size_t)nterms * m * m * 4) + a256((size_t)nterms * n * n * 4) + a256(mn * 4) + a256(mn * 4)) +
          256;
@@ -347,6 +384,39 @@ int kron_term_f32(const float* Ah, const float* Al, const float* Xh, const float
   return rc ? rc : launch_gemm<K_BN, EPI_F32_EMA, default_stages<EPI_F32_EMA>(), 1, 1>(p, st);
 }
 
+// Dense small-factor path (see kron_use_dense): W pair, X pair, one 3xTF32 GEMM.
+int kron_apply_dense_f32(const void* A, int a_trans, const void* X, const void* B, float* Y, int batch, int m, int n,
+                         int nterms, uint8_t* w, cudaStream_t st) {
+  const int mn = m * n;
+  const size_t wbytes = (size_t)mn * mn * 4, xbytes = (size_t)batch * mn * 4;
+  float* Wh = reinterpret_cast<float*>(w);
+  float* Wl = reinterpret_cast<float*>(w + a256(wbytes));
+  float* Xh = reinterpret_cast<float*>(w + 2 * a256(wbytes));
+  float* Xl = reinterpret_cast<float*>(w + 2 * a256(wbytes) + a256(xbytes));
+  {
+    const long long total = (long long)mn * mn;
+    const int blocks = (int)std::min<long long>((total + SPLIT_THREADS - 1) / SPLIT_THREADS, 148LL * 16);
+    ProfScope prof(PK_EW_OTHER, st);
+    kron_dense_w_kernel<<<blocks, SPLIT_THREADS, 0, st>>>(static_cast<const float*>(A), a_trans,
+                                                          static_cast<const float*>(B), m, n, nterms, Wh, Wl);
+    if (launch_ok()) return LSR_ERR_LAUNCH;
+  }
+  int rc = split_tf32(static_cast<const float*>(X), Xh, Xl, (long long)batch * mn, st);
+  if (rc) return rc;
+  GemmParams p{};
+  p.ngroups = 1;
+  GroupDesc& G = p.g[0];
+  set_out(G, 1, batch, mn, Y, nullptr, 0);
+  // Y[r][c] = sum_k X[r][k] W[c][k]: both operands K-major; hi*hi in slot 0, the corrections in slot 1
+  const Operand pr[3][2] = {{mat(Xh, batch, mn, 1, 0, 1), mat(Wh, mn, mn, 1, 0, 1)},
+                            {mat(Xh, batch, mn, 1, 0, 1), mat(Wl, mn, mn, 1, 0, 1)},
+                            {mat(Xl, batch, mn, 1, 0, 1), mat(Wh, mn, mn, 1, 0, 1)}};
+  const SegDesc sd{cdiv(mn, BK_TF32), 0, 0, 0, 0, 0}, sc{cdiv(mn, BK_TF32), 0, 0, 0, 0, 1};
+  const SegDesc sg[3] = {sd, sc, sc};
+  rc = set_segments(p, pr, sg, 3);
+  return rc ? rc : launch_gemm<K_BN, EPI_STORE_F32, default_stages<EPI_STORE_F32>(), 1, 1>(p, st);
+}
+
 int kron_apply(const void* A, int a_trans, const void* X, const void* B, float* Y, int batch, int m, int n,
                int nterms, int f32, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (!kron_dims_ok(batch, m, n, nterms)) return LSR_ERR_ARG;
@@ -367,6 +437,7 @@ int kron_apply(const void* A, int a_trans, const void* X, const void* B, float* 
     }
     return rc;
   }
+  if (kron_use_dense(m, n)) return kron_apply_dense_f32(A, a_trans, X, B, Y, batch, m, n, nterms, w, st);
   float* Ah = reinterpret_cast<float*>(w);
   float* Al = reinterpret_cast<float*>(w += a256((size_t)nterms * m * m * 4));
   float* Bh = reinterpret_cast<float*>(w += a256((size_t)nterms * m * m * 4));
@@ -393,6 +464,45 @@ int kron_apply(const void* A, int a_trans, const void* X, const void* B, float* 
 }  // namespace lsr
 
 extern "C" {
+
+size_t lsr_gemm_f32_workspace_bytes(int batch, int M, int N, int K) {
+  if (batch < 0 || M <= 0 || N <= 0 || K <= 0) return 0;
+  const size_t b = (size_t)std::max(batch, 1);
+  return 2 * a256(b * M * K * 4) + 2 * a256(b * N * K * 4) + 256;  // tf32 pairs of A and of B^T
+}
+
+int lsr_gemm_f32(const float* A, const float* B, float* C, int batch, int M, int N, int K, float alpha, void* ws,
+                 size_t ws_bytes, lsr_stream_t stream) {
+  if (batch < 0 || batch > 65535 || M <= 0 || N <= 0 || K <= 0) return LSR_ERR_ARG;
+  if (batch == 0) return LSR_OK;
+  if (!A || !B || !C) return LSR_ERR_ARG;
+  if (K % 4 || N % 4) return LSR_ERR_SHAPE;  // 16-byte rows for the tensor maps
+  int rc = check_device();
+  if (rc) return rc;
+  if (!ws || ws_bytes < lsr_gemm_f32_workspace_bytes(batch, M, N, K)) return LSR_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* w = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(ws), 256));
+  const size_t ab = a256((size_t)batch * M * K * 4), bb = a256((size_t)batch * N * K * 4);
+  float* Ah = reinterpret_cast<float*>(w);
+  float* Al = reinterpret_cast<float*>(w + ab);
+  float* Bh = reinterpret_cast<float*>(w + 2 * ab);
+  float* Bl = reinterpret_cast<float*>(w + 2 * ab + bb);
+  rc = split_tf32(A, Ah, Al, (long long)batch * M * K, st);
+  if (!rc) rc = split_tf32_t(B, Bh, Bl, batch, K, N, st);  // B^T pair, [batch][N][K]
+  if (rc) return rc;
+  GemmParams p{};
+  p.ngroups = 1;
+  GroupDesc& G = p.g[0];
+  set_out(G, batch, M, N, C, nullptr, 0);
+  G.alpha = alpha;
+  const Operand pr[3][2] = {{mat(Ah, M, K, batch, 0, 1), mat(Bh, N, K, batch, 0, 1)},
+                            {mat(Ah, M, K, batch, 0, 1), mat(Bl, N, K, batch, 0, 1)},
+                            {mat(Al, M, K, batch, 0, 1), mat(Bh, N, K, batch, 0, 1)}};
+  const SegDesc sd{cdiv(K, BK_TF32), 0, 0, 0, 0, 0}, sc{cdiv(K, BK_TF32), 0, 0, 0, 0, 1};
+  const SegDesc sg[3] = {sd, sc, sc};
+  rc = set_segments(p, pr, sg, 3);
+  return rc ? rc : launch_gemm<K_BN, EPI_STORE_F32, default_stages<EPI_STORE_F32>(), 1, 1>(p, st);
+}
 
 int lsr_kron_apply_bf16(const void* A, int a_trans, const void* X, const void* B, float* Y, int batch, int m, int n,
                         int nterms, void* ws, size_t ws_bytes, lsr_stream_t stream) {

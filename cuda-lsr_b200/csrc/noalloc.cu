@@ -19,6 +19,8 @@
 //   * its device address is looked up once per device, on the first call made
 //     with that device current; make that first call before any stream
 //     capture.
+#include <atomic>
+
 #include "runtime.cuh"
 
 #define LSR_NOALLOC_SCRATCH_BYTES (24u << 20)
@@ -33,18 +35,23 @@ namespace {
 static __device__ __align__(256) uint8_t g_noalloc_scratch[LSR_NOALLOC_SCRATCH_BYTES];
 
 constexpr int kMaxDev = 64;
-uint8_t* g_scratch_addr[kMaxDev] = {nullptr};
+// Per-device cache of the array's device address. Atomic so that host threads
+// making their first call on one device at the same time do not race; both
+// look the address up and store the same value.
+std::atomic<uint8_t*> g_scratch_addr[kMaxDev] = {};
 
 // Device address of the scratch array for the current device (nullptr on failure).
 uint8_t* scratch_for_current_device() {
   int d = -1;
   if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kMaxDev) return nullptr;
-  if (!g_scratch_addr[d]) {
+  uint8_t* addr = g_scratch_addr[d].load(std::memory_order_relaxed);
+  if (!addr) {
     void* ptr = nullptr;
     if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) return nullptr;
-    g_scratch_addr[d] = static_cast<uint8_t*>(ptr);
+    addr = static_cast<uint8_t*>(ptr);
+    g_scratch_addr[d].store(addr, std::memory_order_relaxed);
   }
-  return g_scratch_addr[d];
+  return addr;
 }
 
 }  // namespace

@@ -24,16 +24,18 @@ __device__ unsigned int g_tile_sched[2 * kSchedSlots];
 
 namespace {
 constexpr int kMaxDevices = 64;
-int* g_status_cache[kMaxDevices] = {nullptr};
-unsigned int* g_sched_cache[kMaxDevices] = {nullptr};
+// Per-device caches filled on first use. Atomic (relaxed): host threads that
+// fill the same entry at once look up and store the same value.
+std::atomic<int*> g_status_cache[kMaxDevices] = {};
+std::atomic<unsigned int*> g_sched_cache[kMaxDevices] = {};
 std::atomic<unsigned int> g_sched_next{0};
-int g_sm_cache[kMaxDevices] = {0};
-int g_cc_cache[kMaxDevices] = {0};
+std::atomic<int> g_sm_cache[kMaxDevices] = {};
+std::atomic<int> g_cc_cache[kMaxDevices] = {};
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-EncodeTiledFn g_encode = nullptr;
+std::atomic<EncodeTiledFn> g_encode{nullptr};
 
 int current_device() {
   int d = 0;
@@ -91,59 +93,66 @@ void prof_end(int kind, cudaStream_t st) {
 int* status_ptr() {
   const int d = current_device();
   if (d < 0) return nullptr;
-  if (!g_status_cache[d]) {
+  int* s = g_status_cache[d].load(std::memory_order_relaxed);
+  if (!s) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
-    g_status_cache[d] = static_cast<int*>(p);
+    s = static_cast<int*>(p);
+    g_status_cache[d].store(s, std::memory_order_relaxed);
   }
-  return g_status_cache[d];
+  return s;
 }
 
 unsigned int* sched_slot() {
   const int d = current_device();
   if (d < 0) return nullptr;
-  if (!g_sched_cache[d]) {
+  unsigned int* base = g_sched_cache[d].load(std::memory_order_relaxed);
+  if (!base) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_tile_sched) != cudaSuccess) return nullptr;
-    g_sched_cache[d] = static_cast<unsigned int*>(p);
+    base = static_cast<unsigned int*>(p);
+    g_sched_cache[d].store(base, std::memory_order_relaxed);
   }
   const unsigned int k = g_sched_next.fetch_add(1, std::memory_order_relaxed) % kSchedSlots;
-  return g_sched_cache[d] + 2 * k;
+  return base + 2 * k;
 }
 
 int device_sm_count() {
   const int d = current_device();
   if (d < 0) return 1;
-  if (!g_sm_cache[d]) {
-    int n = 0;
+  int n = g_sm_cache[d].load(std::memory_order_relaxed);
+  if (!n) {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
-    g_sm_cache[d] = n > 0 ? n : 1;
+    n = n > 0 ? n : 1;
+    g_sm_cache[d].store(n, std::memory_order_relaxed);
   }
-  return g_sm_cache[d];
+  return n;
 }
 
 int check_device() {
   const int d = current_device();
   if (d < 0) return LSR_ERR_DEVICE;
-  if (!g_cc_cache[d]) {
-    int major = 0;
+  int major = g_cc_cache[d].load(std::memory_order_relaxed);
+  if (!major) {
     if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, d) != cudaSuccess) return LSR_ERR_DEVICE;
-    g_cc_cache[d] = major;
+    g_cc_cache[d].store(major, std::memory_order_relaxed);
   }
-  return g_cc_cache[d] == 10 ? LSR_OK : LSR_ERR_DEVICE;
+  return major == 10 ? LSR_OK : LSR_ERR_DEVICE;
 }
 
 int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t inner,
                    uint64_t outer, uint64_t batch, uint64_t ld, uint64_t bstride, uint32_t box_inner,
                    uint32_t box_outer, CUtensorMapSwizzle swizzle) {
-  if (!g_encode) {
+  EncodeTiledFn encode = g_encode.load(std::memory_order_relaxed);
+  if (!encode) {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) !=
             cudaSuccess ||
         q != cudaDriverEntryPointSuccess || !fn)
       return LSR_ERR_DRIVER;
-    g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    encode = reinterpret_cast<EncodeTiledFn>(fn);
+    g_encode.store(encode, std::memory_order_relaxed);
   }
   // TMA requirements: 16-byte aligned base and strides.
   if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * elem_bytes) & 15) || ((bstride * elem_bytes) & 15))
@@ -152,7 +161,7 @@ int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, 
   cuuint64_t strides[2] = {ld * elem_bytes, bstride * elem_bytes};
   cuuint32_t box[3] = {box_inner, box_outer, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = g_encode(map, dtype, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  CUresult r = encode(map, dtype, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? LSR_OK : LSR_ERR_DRIVER;

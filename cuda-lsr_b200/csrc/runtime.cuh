@@ -114,7 +114,8 @@ inline void setup_out_map(GemmParams& p, int g) {
   auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   if (EPI == EPI_SOAP_ADAM) {  // coalesced staged path without TMA: 16-byte m / v, 8-byte u vectors
     G.tma_out = (G.N % 4 == 0) && (G.ldo % 4 == 0) && (G.out_bs % 4 == 0) && a16(G.st_m) && a16(G.st_v) &&
-                ((reinterpret_cast<uintptr_t>(G.out) & 7) == 0);
+                ((reinterpret_cast<uintptr_t>(G.out) & 7) == 0) &&
+                ((reinterpret_cast<uintptr_t>(G.out2) & 7) == 0);
     return;
   }
   if (!G.out || !a16(G.out) || (G.ldo * T::ESZ) % 16 || (G.out_bs * T::ESZ) % 16 || G.N % T::EPV) return;

@@ -16,6 +16,7 @@ import torch
 LIB_PATH = Path(__file__).resolve().parent / "liblsr.so"
 
 LSR_OK = 0
+DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}  # LSR_DTYPE_* (include/lsr.h)
 _ERRORS = {
     -1: ValueError,
     -2: ValueError,
@@ -93,6 +94,21 @@ SIGNATURES: dict[str, tuple] = {
          c_size_t, c_void_p]),
     "lsr_blocks_gather_bf16": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "lsr_blocks_apply_bf16": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_float, c_float, c_void_p]),
+    "lsr_blocks_apply_any": (
+        c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_float, c_float, c_void_p]),
+    "lsr_graft_tiles": (c_int, [c_int, c_int]),
+    "lsr_shampoo_graft_prepare_bf16": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float,
+                c_float, c_int, c_void_p]),
+    "lsr_shampoo_graft_scale_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "lsr_gemm_f32_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "lsr_gemm_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float, c_void_p, c_size_t,
+                             c_void_p]),
+    "lsr_qr_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "lsr_householder_qr_f32": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "lsr_eigenbasis_refresh_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "lsr_eigenbasis_refresh_f32": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "lsr_coupled_newton_workspace_bytes": (c_size_t, [c_int, c_int]),
     "lsr_coupled_newton_f32": (
         c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float, c_int,

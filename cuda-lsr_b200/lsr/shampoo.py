@@ -19,13 +19,16 @@ config objects and runs the preconditioner math in liblsr:
 * SOAP direction Q_L^T G Q_R -> Adam (m, v in the rotated basis) -> Q_L U' Q_R^T:
   ``lsr_soap_direction_bf16``;
 * decoupled weight decay and the update: ``lsr_blocks_apply_bf16``;
-* every ``precondition_frequency`` steps from ``start_preconditioning_step``
-  the inverse roots / eigenbases are recomputed from L, R with an fp32
-  eigendecomposition (``torch.linalg.eigh``, the periodic step; before the
-  first one Shampoo uses the grafting direction and SOAP the identity basis);
-  ``root_inverse_method="coupled_newton"`` computes Shampoo's inverse 4th
-  roots with the batched coupled Newton kernel instead (``lsr.newton``, the
-  recurrence of shampoo.py:277-542, all blocks of one shape in one call);
+* at every multiple of ``precondition_frequency`` from
+  ``start_preconditioning_step`` on (the reference's periodic steps) the
+  inverse roots / eigenbases are recomputed from L, R (before the first one
+  Shampoo uses the grafting direction and SOAP the identity basis): SOAP's
+  eigenbases by power iteration with a Householder QR from the current basis
+  (``lsr_eigenbasis_refresh_f32``; ``amortized_computation=False`` uses an fp32
+  ``torch.linalg.eigh`` instead), Shampoo's inverse 4th roots by the batched
+  coupled Newton kernel (``lsr.newton``, the recurrence of shampoo.py:277-542,
+  all blocks of one shape in one call; ``root_inverse_method="eigh"`` uses an
+  eigendecomposition instead);
 * with ``DDPDistributedConfig`` and an initialised process group the blocks
   are owned by ranks (greedy by flops, ZeRO-1: state only for owned blocks),
   directions are all-gathered in ``communication_dtype`` and every rank
@@ -59,15 +62,24 @@ class AdamPreconditionerConfig:
 
 @dataclass
 class DDPDistributedConfig:
-    communication_dtype: torch.dtype = torch.float32
+    # float16, the reference script's default (shampoo_soap_lm_ddp_zero1.py:429-434)
+    communication_dtype: torch.dtype = torch.float16
     num_trainers_per_group: int = -1
     communicate_params: bool = False
 
 
 @dataclass
 class EigenvalueCorrectedShampooConfig:
-    """SOAP: Adam in the eigenbasis of the Shampoo factors."""
+    """SOAP: Adam in the eigenbasis of the Shampoo factors.
+
+    amortized_computation=True (the default, as DefaultSOAPConfig's amortized eigenbasis
+    computation): every refresh takes ``max_iterations`` steps of power iteration with a
+    Householder QR from the current basis (``first_iterations`` on the first refresh, which
+    starts from the identity), on liblsr's kernels (lsr_eigenbasis_refresh_f32).
+    amortized_computation=False: an fp32 eigendecomposition per refresh (torch.linalg.eigh)."""
     amortized_computation: bool = True
+    max_iterations: int = 1
+    first_iterations: int = 4
 
 
 DefaultSOAPConfig = EigenvalueCorrectedShampooConfig()
@@ -118,6 +130,7 @@ class _BlockGroup:
         eye_r = torch.eye(r, device=device, dtype=torch.bfloat16).expand(n, r, r).contiguous()
         eye_c = torch.eye(c, device=device, dtype=torch.bfloat16).expand(n, c, c).contiguous()
         self.QL, self.QR = eye_r, eye_c  # SOAP eigenbases or Shampoo inverse roots (bf16)
+        self.QLf = self.QRf = None  # SOAP: fp32 master bases of the amortized refresh
         self.have_roots = False
         self.m = torch.zeros(n, r, c, dtype=torch.float32, device=device)  # SOAP m / Shampoo filtered grad
         self.v = torch.zeros(n, r, c, dtype=torch.float32, device=device)  # SOAP v / grafting v
@@ -125,6 +138,7 @@ class _BlockGroup:
         self.U = torch.empty(n, r, c, dtype=torch.float32, device=device)
         self._ptr_key = None
         self._grad_key = None
+        self.adam_sq = self.u_sq = self.gf = None  # Shampoo grafting buffers, made on first use
 
     def pointers(self):
         """Device arrays of the blocks' parameter and gradient addresses and row strides,
@@ -149,7 +163,7 @@ class DistributedShampoo(torch.optim.Optimizer):
                  max_preconditioner_dim=1024, precondition_frequency=1, start_preconditioning_step=-1,
                  weight_decay_type=WeightDecayType.DECOUPLED, distributed_config: Optional[DDPDistributedConfig] = None,
                  grafting_config: Optional[AdamPreconditionerConfig] = None, preconditioner_config=None,
-                 eager_nan_check: bool = False, root_inverse_method: str = "eigh", **unused):
+                 eager_nan_check: bool = False, root_inverse_method: str = "coupled_newton", **unused):
         if weight_decay_type != WeightDecayType.DECOUPLED:
             raise ValueError("only WeightDecayType.DECOUPLED is supported")
         if max_preconditioner_dim % 8:
@@ -157,6 +171,7 @@ class DistributedShampoo(torch.optim.Optimizer):
         defaults = dict(lr=lr, betas=betas, epsilon=epsilon, weight_decay=weight_decay)
         super().__init__(params, defaults)
         self.soap = isinstance(preconditioner_config, EigenvalueCorrectedShampooConfig)
+        self.soap_cfg = preconditioner_config if self.soap else None
         if root_inverse_method not in ("eigh", "coupled_newton"):
             raise ValueError(f"root_inverse_method must be 'eigh' or 'coupled_newton', got {root_inverse_method!r}")
         self.root_inverse_method = root_inverse_method
@@ -170,6 +185,11 @@ class DistributedShampoo(torch.optim.Optimizer):
         self.step_count = 0
         self._groups = None
         self._comm_dtype = distributed_config.communication_dtype if distributed_config else torch.float32
+        if self._comm_dtype not in _lib.DTYPE_CODES:
+            raise ValueError(f"communication_dtype must be float32, bfloat16 or float16, got {self._comm_dtype}")
+        self._ex: dict = {}
+        self._comm_stream = None
+        self._pending_comm = False
 
     # ------------------------------------------------------------------ setup
     def _matrix_params(self):
@@ -197,7 +217,9 @@ class DistributedShampoo(torch.optim.Optimizer):
             by_shape.setdefault((e[3], e[4]), []).append((e, o))
         self._groups = []
         self._all_blocks = {}
-        for shape, lst in sorted(by_shape.items()):
+        # largest block shapes first: the exchange left after the last shape's compute is the smallest
+        for shape, lst in sorted(by_shape.items(), key=lambda kv: (-kv[0][0] * kv[0][1] * (kv[0][0] + kv[0][1]),
+                                                                    kv[0])):
             owned = [(e[0], e[1], e[2]) for e, o in lst if o == self.rank]
             grp = _BlockGroup(shape, owned, entries[0][0].device, self.soap) if owned else None
             self._groups.append((shape, grp, lst))
@@ -205,9 +227,11 @@ class DistributedShampoo(torch.optim.Optimizer):
     # ------------------------------------------------------------------ periodic refresh
     def _refresh(self, grp: _BlockGroup, eps: float):
         r, c = grp.shape
-        eye_r = torch.eye(r, device=grp.L.device)
-        eye_c = torch.eye(c, device=grp.R.device)
-        if self.soap:
+        if self.soap and self.soap_cfg.amortized_computation:
+            self._refresh_amortized(grp, eps)
+        elif self.soap:
+            eye_r = torch.eye(r, device=grp.L.device)
+            eye_c = torch.eye(c, device=grp.R.device)
             _, QL = torch.linalg.eigh(grp.L + eps * eye_r)
             _, QR = torch.linalg.eigh(grp.R + eps * eye_c)
             grp.QL, grp.QR = QL.bfloat16().contiguous(), QR.bfloat16().contiguous()
@@ -216,12 +240,46 @@ class DistributedShampoo(torch.optim.Optimizer):
             grp.QL = batched_coupled_newton(grp.L, 4, epsilon=eps)[0].bfloat16().contiguous()
             grp.QR = batched_coupled_newton(grp.R, 4, epsilon=eps)[0].bfloat16().contiguous()
         else:
+            eye_r = torch.eye(r, device=grp.L.device)
+            eye_c = torch.eye(c, device=grp.R.device)
+
             def root(S, I):
                 w, V = torch.linalg.eigh(S + eps * I)
                 return (V * w.clamp_min(1e-30).pow(-0.25).unsqueeze(-2)) @ V.transpose(-1, -2)
             grp.QL = root(grp.L, eye_r).bfloat16().contiguous()
             grp.QR = root(grp.R, eye_c).bfloat16().contiguous()
         grp.have_roots = True
+
+    # blocks per refresh call: bounds the transient workspace (the W buffer and the
+    # tf32 pairs of the fp32 GEMM, about 6 n^2 fp32 values per block)
+    REFRESH_CHUNK = 128
+
+    def _refresh_amortized(self, grp: _BlockGroup, eps: float):
+        """Power iteration with Householder QR on liblsr's kernels, from the fp32 master bases
+        (identity before the first refresh); bf16 copies for the SOAP chain."""
+        lib = _lib.load()
+        n = len(grp.refs)
+        first = grp.QLf is None
+        if first:
+            grp.QLf = torch.empty(n, grp.shape[0], grp.shape[0], dtype=torch.float32, device=grp.L.device)
+            grp.QRf = torch.empty(n, grp.shape[1], grp.shape[1], dtype=torch.float32, device=grp.R.device)
+        iters = self.soap_cfg.first_iterations if first else self.soap_cfg.max_iterations
+        st = _lib.stream_handle(grp.L.device)
+        for S, Qf, Qb in ((grp.L, grp.QLf, grp.QL), (grp.R, grp.QRf, grp.QR)):
+            k = S.shape[-1]
+            for b0 in range(0, n, self.REFRESH_CHUNK):
+                nb_ = min(self.REFRESH_CHUNK, n - b0)
+                nbytes = lib.lsr_eigenbasis_refresh_workspace_bytes(nb_, k)
+                ws = _lib.WORKSPACE.get(nbytes, S.device)
+                _lib.check(lib.lsr_eigenbasis_refresh_f32(
+                    S[b0:b0 + nb_].data_ptr(), Qf[b0:b0 + nb_].data_ptr(), Qb[b0:b0 + nb_].data_ptr(), nb_, k, eps,
+                    int(first), max(1, iters), ws.data_ptr(), nbytes, st), "lsr_eigenbasis_refresh_f32")
+
+    def is_refresh_step(self, t: int) -> bool:
+        """True when 1-based step t recomputes the roots / eigenbases: from the start step on, at every
+        multiple of the frequency (every step when it is 1). This is the schedule the reference times
+        as its periodic steps (shampoo_soap_lm_ddp_zero1.py:622-632)."""
+        return t >= self.start and (t % self.freq == 0 or self.freq == 1)
 
     # ------------------------------------------------------------------ step
     @torch.no_grad()
@@ -238,7 +296,7 @@ class DistributedShampoo(torch.optim.Optimizer):
         lr, (b1, b2), eps, wd = g0["lr"], g0["betas"], g0["epsilon"], g0["weight_decay"]
         lib = _lib.load()
         precondition = t >= self.start
-        refresh = precondition and (t - self.start) % self.freq == 0
+        refresh = self.is_refresh_step(t)
         for shape, grp, lst in self._groups:
             r, c = shape
             if grp is not None:
@@ -264,35 +322,71 @@ class DistributedShampoo(torch.optim.Optimizer):
                 else:
                     self._shampoo_direction(grp, n, r, c, b1, t, precondition and grp.have_roots)
             self._exchange_and_apply(shape, grp, lst, lr, wd)
+        if self._pending_comm:
+            # the send buffers are rewritten by the next step and the parameters read by what follows:
+            # the compute stream waits for every exchange and apply of this step
+            torch.cuda.current_stream().wait_stream(self._comm_stream)
+            self._pending_comm = False
         self._adam_non_matrix(t)
         return loss
 
     def _shampoo_direction(self, grp, n, r, c, b1, t, precondition):
-        """First-moment filter, Adam grafting and (after the start step) the Shampoo direction."""
+        """First-moment filter, Adam grafting and (after the first inverse roots) the grafted Shampoo
+        direction, all in liblsr: the prepare pass updates m, v and writes the filtered gradient (bf16,
+        the apply's operand) and the per-block Adam norms; the apply runs L^-1/4 Gf R^-1/4; the scale
+        pass gives each block the Frobenius norm of its Adam direction."""
         lib = _lib.load()
+        st = _lib.stream_handle(grp.stack.device)
+        tiles = lib.lsr_graft_tiles(r, c)
+        if grp.adam_sq is None:
+            dev = grp.stack.device
+            grp.adam_sq = torch.empty(n, tiles, dtype=torch.float32, device=dev)
+            grp.u_sq = torch.empty(n, tiles, dtype=torch.float32, device=dev)
+            grp.gf = torch.empty(n, r, c, dtype=torch.bfloat16, device=dev)
         gb2, geps = self.grafting.beta2, self.grafting.epsilon
-        G = grp.stack.float()
-        grp.v.mul_(gb2).addcmul_(G, G, value=1 - gb2)
-        if b1 > 0:
-            grp.m.mul_(b1).add_(G, alpha=1 - b1)
-            Gf = grp.m / (1 - b1 ** t)
-        else:
-            Gf = G
-        adam = Gf / ((grp.v / (1 - gb2 ** t)).sqrt() + geps)
+        _lib.check(lib.lsr_shampoo_graft_prepare_bf16(
+            grp.stack.data_ptr(), grp.m.data_ptr() if b1 > 0 else None, grp.v.data_ptr(), grp.gf.data_ptr(),
+            None if precondition else grp.U.data_ptr(), grp.adam_sq.data_ptr(), n, r, c, b1, gb2, geps, t, st),
+            "lsr_shampoo_graft_prepare_bf16")
         if not precondition:
-            grp.U.copy_(adam)
             return
-        Gfb = Gf.bfloat16().contiguous()
         nb = lib.lsr_shampoo_workspace_bytes(n, r, c)
-        ws = _lib.WORKSPACE.get(nb, Gfb.device)
-        _lib.check(lib.lsr_shampoo_direction_bf16(Gfb.data_ptr(), None, None, grp.QL.data_ptr(), grp.QR.data_ptr(),
-                                                  grp.U.data_ptr(), n, r, c, 0.0, 0, ws.data_ptr(), nb,
-                                                  _lib.stream_handle(Gfb.device)), "lsr_shampoo_direction_bf16")
-        # per-block norms accumulated in fp64: torch picks its reduction order from the stack's shape,
-        # and this keeps a block's scale independent of which blocks share its stack
-        scale = (adam.double().flatten(1).norm(dim=1) /
-                 grp.U.double().flatten(1).norm(dim=1).clamp_min(1e-30)).float()
-        grp.U.mul_(scale[:, None, None])
+        ws = _lib.WORKSPACE.get(nb, grp.stack.device)
+        _lib.check(lib.lsr_shampoo_direction_bf16(grp.gf.data_ptr(), None, None, grp.QL.data_ptr(), grp.QR.data_ptr(),
+                                                  grp.U.data_ptr(), n, r, c, 0.0, 0, ws.data_ptr(), nb, st),
+                   "lsr_shampoo_direction_bf16")
+        _lib.check(lib.lsr_shampoo_graft_scale_f32(grp.U.data_ptr(), grp.adam_sq.data_ptr(), grp.u_sq.data_ptr(),
+                                                   n, r, c, st), "lsr_shampoo_graft_scale_f32")
+
+    def _exchange_state(self, shape, lst):
+        """Persistent ZeRO-1 exchange buffers of one block shape: send [per][r][c] and recv
+        [world*per][r][c] in the communication dtype (padding slots stay zero), and the device arrays
+        that map every real recv slot to its parameter block (address, row stride, slot index)."""
+        st = self._ex.get(shape)
+        if st is not None and st["key"] == tuple(e[0].data_ptr() for e, _ in lst):
+            return st
+        r, c = shape
+        dev = lst[0][0][0].device
+        counts = [sum(1 for _, o in lst if o == k) for k in range(self.world)]
+        per = max(counts)
+        refs, slots = [], []
+        for k in range(self.world):
+            mine = [e for e, o in lst if o == k]
+            for j, e in enumerate(mine):
+                refs.append(e)
+                slots.append(k * per + j)
+        st = {
+            "key": tuple(e[0].data_ptr() for e, _ in lst),
+            "send": torch.zeros(per, r, c, dtype=self._comm_dtype, device=dev),
+            "recv": torch.empty(self.world * per, r, c, dtype=self._comm_dtype, device=dev),
+            "ptrs": torch.tensor([e[0].data_ptr() + 2 * (e[1] * e[0].shape[1] + e[2]) for e in refs],
+                                 dtype=torch.int64).to(dev),
+            "lds": torch.tensor([e[0].shape[1] for e in refs], dtype=torch.int32).to(dev),
+            "slots": torch.tensor(slots, dtype=torch.int32).to(dev),
+            "n": len(refs),
+        }
+        self._ex[shape] = st
+        return st
 
     def _exchange_and_apply(self, shape, grp, lst, lr, wd):
         lib = _lib.load()
@@ -303,27 +397,26 @@ class DistributedShampoo(torch.optim.Optimizer):
                                                  grp.U.data_ptr(), lr, wd, _lib.stream_handle(grp.U.device)),
                        "lsr_blocks_apply_bf16")
             return
-        # ZeRO-1: gather every rank's directions for this block shape, apply all of them
-        counts = [sum(1 for _, o in lst if o == k) for k in range(self.world)]
-        per = max(counts)
-        dev = lst[0][0][0].device
-        send = torch.zeros(per, r, c, dtype=self._comm_dtype, device=dev)
+        # ZeRO-1: this rank's directions go into the persistent send buffer (in the communication dtype)
+        # on the compute stream; the all-gather and the apply of every rank's directions run on the comm
+        # stream, overlapped with the next block shape's compute.
+        ex = self._exchange_state(shape, lst)
+        compute = torch.cuda.current_stream()
         if grp is not None:
-            send[:len(grp.refs)].copy_(grp.U)
-        recv = torch.empty(self.world * per, r, c, dtype=self._comm_dtype, device=dev)
-        dist.all_gather_into_tensor(recv, send)
-        refs, U = [], []
-        for k in range(self.world):
-            mine = [e for e, o in lst if o == k]
-            for j, e in enumerate(mine):
-                refs.append(e)
-                U.append(k * per + j)
-        Uall = recv[torch.tensor(U, device=dev)].float().contiguous()
-        ptrs = torch.tensor([e[0].data_ptr() + 2 * (e[1] * e[0].shape[1] + e[2]) for e in refs],
-                            dtype=torch.int64).to(dev)
-        lds = torch.tensor([e[0].shape[1] for e in refs], dtype=torch.int32).to(dev)
-        _lib.check(lib.lsr_blocks_apply_bf16(ptrs.data_ptr(), lds.data_ptr(), len(refs), r, c, Uall.data_ptr(), lr, wd,
-                                             _lib.stream_handle(dev)), "lsr_blocks_apply_bf16")
+            ex["send"][:len(grp.refs)].copy_(grp.U)
+        if self._comm_stream is None:
+            self._comm_stream = torch.cuda.Stream(device=compute.device)
+        comm = self._comm_stream
+        ev = torch.cuda.Event()
+        ev.record(compute)
+        comm.wait_event(ev)
+        with torch.cuda.stream(comm):
+            dist.all_gather_into_tensor(ex["recv"], ex["send"])
+            _lib.check(lib.lsr_blocks_apply_any(ex["ptrs"].data_ptr(), ex["lds"].data_ptr(), ex["n"], r, c,
+                                                ex["recv"].data_ptr(), _lib.DTYPE_CODES[self._comm_dtype],
+                                                ex["slots"].data_ptr(), lr, wd, comm.cuda_stream),
+                       "lsr_blocks_apply_any")
+        self._pending_comm = True
 
     def _adam_non_matrix(self, t):
         gb2, geps = self.grafting.beta2, self.grafting.epsilon

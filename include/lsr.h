@@ -44,6 +44,11 @@ typedef struct CUstream_st* lsr_stream_t; /* == cudaStream_t */
 #define LSR_ERR_TOO_LARGE (-7) /* problem exceeds the fixed scratch capacity */
 #define LSR_ERR_PEER (-8)      /* CUDA IPC / peer memory call failed         */
 
+/* Element types of lsr_blocks_apply_any's update operand. */
+#define LSR_DTYPE_F32 0
+#define LSR_DTYPE_BF16 1
+#define LSR_DTYPE_F16 2
+
 /* Library version string, e.g. "lsr-b200 0.1.0 (sm_100a)". */
 LSR_API const char* lsr_version(void);
 
@@ -190,6 +195,40 @@ LSR_API int lsr_gram_update_f32(const void* G, void* S, int batch, int rows, int
                                 float alpha, lsr_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * fp32 batched GEMM on the tensor cores: C[b] = alpha A[b] B[b] with A [M][K],
+ * B [K][N], C [M][N] row-major fp32, evaluated as 3xTF32 (hi*hi + hi*lo +
+ * lo*hi of the tf32 splits, corrections in a second accumulator): fp32-level
+ * accuracy. Replaces the reference's fp32 torch.matmul / bmm products of its
+ * preconditioner code (the coupled-Newton products, shampoo.py:408-542; the
+ * two-sided apply, hft.py:108-140). K and N multiples of 4.
+ * ---------------------------------------------------------------------- */
+LSR_API size_t lsr_gemm_f32_workspace_bytes(int batch, int M, int N, int K);
+LSR_API int lsr_gemm_f32(const float* A, const float* B, float* C, int batch, int M, int N, int K, float alpha,
+                         void* ws, size_t ws_bytes, lsr_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Batched Householder QR of square fp32 matrices, n <= 1024:
+ *   W[b] = Q[b] R[b], Q written to Q (W is overwritten by R and the
+ *   Householder vectors), column signs chosen so that diag(R) >= 0.
+ * SOAP eigenbasis refresh (the periodic, amortized eigenbasis computation of
+ * DefaultSOAPConfig in the third-party distributed_shampoo, whose periodic
+ * steps shampoo_soap_lm_ddp_zero1.py:622-653 times): `iterations` steps of
+ * power iteration on each factor S[b] (n x n, fp32, symmetric):
+ *   W = (S + eps I) Qf  (from_identity: W = S + eps I on the first step),
+ *   Qf = qr(W).Q;
+ * Qf [b][n][n] fp32 is the basis in and out; Qb, if not null, receives its
+ * bf16 copy (the operand of lsr_soap_direction_bf16). Because diag(R) >= 0
+ * a converged basis comes back unchanged, without column sign flips.
+ * ---------------------------------------------------------------------- */
+LSR_API size_t lsr_qr_workspace_bytes(int batch, int n);
+LSR_API int lsr_householder_qr_f32(float* W, float* Q, int batch, int n, void* ws, size_t ws_bytes,
+                                   lsr_stream_t stream);
+LSR_API size_t lsr_eigenbasis_refresh_workspace_bytes(int batch, int n);
+LSR_API int lsr_eigenbasis_refresh_f32(const float* S, float* Qf, void* Qb, int batch, int n, float eps,
+                                       int from_identity, int iterations, void* ws, size_t ws_bytes,
+                                       lsr_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Kronecker sum  (A ⊕ B) vec(X) = vec(A X + X B^T), row-major vec, batched
  * over X [batch][m][n]; A (m x m) and B (n x n) shared by the batch; Y is
  * fp32 [batch][m][n]. One fused kernel: both products accumulate in the same
@@ -253,9 +292,11 @@ LSR_API int lsr_kron_reconstruct_f32(const float* const* factors, const int* row
  *   then G' = Q_L^T G Q_R and Adam in that basis (fused into the rotation):
  *     m = beta1 m + (1-beta1) G',  v = beta2 v + (1-beta2) G'^2,
  *     U' = (m / (1-beta1^step)) / (sqrt(v / (1-beta2^step)) + eps),
- *   and the update direction U = Q_L U' Q_R^T (fp32). Every GEMM operand of
- *   the chain is bf16: the intermediates (G Q_R or Q_L^T G, then U' Q_R^T or
- *   Q_L U', the cheaper association first) and U' are rounded to bf16.
+ *   and the update direction U = Q_L U' Q_R^T (fp32). G, Q_L and Q_R are the
+ *   bf16 operands; every value computed from them that feeds a further GEMM
+ *   (the intermediate of each two-sided product, G Q_R or Q_L^T G and then
+ *   U' Q_R^T or Q_L U', the cheaper association first, and U' itself) is kept
+ *   as a bf16 hi + lo pair, so the result has fp32-level accuracy.
  *   L fp32 [b][r][r], R fp32 [b][c][c], Q_L bf16 [b][r][r], Q_R bf16 [b][c][c],
  *   m, v fp32 [b][r][c]; rows, cols multiples of 8.
  * lsr_shampoo_direction_bf16: optional statistics update as above, then
@@ -281,6 +322,35 @@ LSR_API int lsr_blocks_gather_bf16(const uint64_t* ptrs, const int* lds, int nbl
                                    void* stack, lsr_stream_t stream);
 LSR_API int lsr_blocks_apply_bf16(const uint64_t* ptrs, const int* lds, int nblocks, int rows, int cols,
                                   const float* U, float lr, float weight_decay, lsr_stream_t stream);
+/* As lsr_blocks_apply_bf16 with U of element type u_dtype (LSR_DTYPE_*; the
+ * ZeRO-1 exchange's communication dtype, shampoo_soap_lm_ddp_zero1.py:341-345,
+ * :429-434) and an optional DEVICE index array: block b reads U entry
+ * u_index[b] (b when u_index is null), so an all-gathered buffer with padding
+ * slots is applied in place. */
+LSR_API int lsr_blocks_apply_any(const uint64_t* ptrs, const int* lds, int nblocks, int rows, int cols,
+                                 const void* U, int u_dtype, const int* u_index, float lr, float weight_decay,
+                                 lsr_stream_t stream);
+
+/* Adam grafting of the Shampoo direction (the reference's "shampoo" mode,
+ * grafting_config=AdamPreconditionerConfig(beta2=betas[1], epsilon=1e-8),
+ * shampoo_soap_lm_ddp_zero1.py:347-352), on a gradient stack G [b][r][c] bf16:
+ * lsr_shampoo_graft_prepare_bf16, per element:
+ *     v = gbeta2 v + (1-gbeta2) g^2;
+ *     beta1 > 0: m = beta1 m + (1-beta1) g, gf = m / (1-beta1^step); else gf = g;
+ *     adam = gf / (sqrt(v / (1-gbeta2^step)) + geps);
+ *   Gf = bf16(gf) (the operand of the Shampoo apply), U = adam when U is not
+ *   null (steps before the first inverse roots), and per block the partial sums
+ *   of adam^2, adam_sq [b][lsr_graft_tiles(r, c)].
+ * lsr_shampoo_graft_scale_f32: U[b] *= ||adam_b||_F / max(||U_b||_F, 1e-30),
+ *   the grafted Shampoo direction; u_sq is scratch of the same shape as
+ *   adam_sq. Both norms are summed in a fixed order per block, so a block's
+ *   scale does not depend on which blocks share its stack. m, v fp32 [b][r][c]. */
+LSR_API int lsr_graft_tiles(int rows, int cols);
+LSR_API int lsr_shampoo_graft_prepare_bf16(const void* G, float* m, float* v, void* Gf, float* U, float* adam_sq,
+                                           int batch, int rows, int cols, float beta1, float gbeta2, float geps,
+                                           int step, lsr_stream_t stream);
+LSR_API int lsr_shampoo_graft_scale_f32(float* U, const float* adam_sq, float* u_sq, int batch, int rows, int cols,
+                                        lsr_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Batched coupled Newton inverse roots  X[b] = (A[b] + eps I)^{-1/root}

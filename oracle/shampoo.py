@@ -47,11 +47,21 @@ def shampoo_precondition(G, Lroot, Rroot):
 def soap_direction(G, QL, QR, m, v, beta1, beta2, eps, step, bf16_operands=False):
     """Returns (U, m, v) for one SOAP step in the eigenbases QL, QR.
 
-    bf16_operands=True rounds every GEMM operand to bf16 as the kernels do: the
-    intermediate of each two-sided product (cheaper association first: G Q_R
-    then Q_L^T (.) when cols > rows, else Q_L^T G then (.) Q_R) and the Adam
-    direction U'.
+    Default: float64 arithmetic on the given operands (the caller passes G, QL,
+    QR already rounded to bf16, the only roundings the reference's fp32 path
+    applies to its inputs); this is what the kernels are checked against.
+
+    bf16_operands=True is a diagnostic only: it also rounds every computed GEMM
+    operand to bf16 (the intermediate of each two-sided product, cheaper
+    association first, and the Adam direction U'), which shows how far a chain
+    with plain-bf16 intermediates falls from the default.
     """
+    U, m, v, _ = soap_direction_parts(G, QL, QR, m, v, beta1, beta2, eps, step, bf16_operands)
+    return U, m, v
+
+
+def soap_direction_parts(G, QL, QR, m, v, beta1, beta2, eps, step, bf16_operands=False):
+    """soap_direction that also returns the Adam direction in the rotated basis: (U, m, v, U')."""
     from .bf16 import round_bf16
     rd = (lambda x: round_bf16(np.asarray(x, np.float32)).astype(np.float64)) if bf16_operands else (lambda x: x)
     QL = np.asarray(QL, np.float64)
@@ -62,10 +72,25 @@ def soap_direction(G, QL, QR, m, v, beta1, beta2, eps, step, bf16_operands=False
     Gr = QLt @ rd(G @ QR) if right_first else rd(QLt @ G) @ QR
     m = beta1 * np.asarray(m, np.float64) + (1.0 - beta1) * Gr
     v = beta2 * np.asarray(v, np.float64) + (1.0 - beta2) * Gr * Gr
-    Up = rd((m / (1.0 - beta1 ** step)) / (np.sqrt(v / (1.0 - beta2 ** step)) + eps))
-    QRt = np.swapaxes(QR, -1, -2)
-    U = QL @ rd(Up @ QRt) if right_first else rd(QL @ Up) @ QRt
-    return U, m, v
+    Up = rd(adam_in_basis(m, v, beta1, beta2, eps, step))
+    return soap_rotate_back(Up, QL, QR, bf16_operands), m, v, Up
+
+
+def adam_in_basis(m, v, beta1, beta2, eps, step):
+    """U' = (m / (1 - beta1^t)) / (sqrt(v / (1 - beta2^t)) + eps)."""
+    return (np.asarray(m, np.float64) / (1.0 - beta1 ** step)) / (
+        np.sqrt(np.asarray(v, np.float64) / (1.0 - beta2 ** step)) + eps)
+
+
+def soap_rotate_back(Up, QL, QR, bf16_operands=False):
+    """U = Q_L U' Q_R^T, the cheaper association first."""
+    from .bf16 import round_bf16
+    rd = (lambda x: round_bf16(np.asarray(x, np.float32)).astype(np.float64)) if bf16_operands else (lambda x: x)
+    QL = np.asarray(QL, np.float64)
+    QRt = np.swapaxes(np.asarray(QR, np.float64), -1, -2)
+    Up = np.asarray(Up, np.float64)
+    right_first = Up.shape[-1] > Up.shape[-2]
+    return QL @ rd(Up @ QRt) if right_first else rd(QL @ Up) @ QRt
 
 
 def coupled_newton_one(A, root, epsilon=0.0, tolerance=1e-6, max_iterations=100):

@@ -1,0 +1,72 @@
+"""Stage the reference's own modules for the baselines — TEST INFRASTRUCTURE ONLY.
+
+The reference implements its Muon path in Python / torch (muon_lm_ddp.py:296-696:
+adjusted_muon_lr, zeropower_serial, zeropower_batched_oriented, MuonAdamW),
+so there is nothing to compile, and its Kronecker-sum kernel
+(kron_sum_64x8_kernel, hft_fused.py:89-319) is CUDA source that hft_fused.py
+builds itself with torch's load_inline when imported on a GPU machine. This
+recipe copies those two modules, unmodified, from a cuda-lsr checkout into
+``oracle/_ref/`` (git-ignored; it travels with the working tree to the machine
+that runs the benchmark, where the checkout is absent) and records their
+SHA-256 beside them:
+
+    python oracle/stage_reference.py --reference <path of the cuda-lsr checkout>
+
+``bench.py``'s reference arm and its ``cpu_baseline`` leg import the staged
+Muon module and time the reference's own ``MuonAdamW.muon_step`` on the host
+cores (``cpu_baseline.kind = "reference"``); without it they fall back to the
+numpy restatement in ``oracle/muon.py`` (``kind = "port"``). ``bench.py
+--workload kron64x8`` imports the staged hft_fused.py to time the reference's
+kernel beside liblsr's on the same GPU. Nothing in the product (the ``lsr``
+package) imports them.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import shutil
+import sys
+from pathlib import Path
+
+REF_DIR = Path(__file__).resolve().parent / "_ref"
+MODULE = "muon_lm_ddp.py"
+MODULES = (MODULE, "hft_fused.py")
+
+
+def stage(reference: str | Path) -> Path | None:
+    """Copy the reference's muon_lm_ddp.py and hft_fused.py into oracle/_ref/; returns the staged
+    Muon module's path (None if the checkout has none)."""
+    out = None
+    for name in MODULES:
+        src = Path(reference) / name
+        if not src.is_file():
+            continue
+        REF_DIR.mkdir(exist_ok=True)
+        dst = REF_DIR / name
+        shutil.copyfile(src, dst)
+        digest = hashlib.sha256(dst.read_bytes()).hexdigest()
+        (REF_DIR / (name + ".sha256")).write_text(f"{digest}  {name}\n")
+        if name == MODULE:
+            out = dst
+    return out
+
+
+def staged_module_path(name: str = MODULE) -> Path | None:
+    p = REF_DIR / name
+    return p if p.is_file() else None
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--reference", required=True, help="path of the cuda-lsr checkout")
+    args = ap.parse_args(argv)
+    out = stage(args.reference)
+    if out is None:
+        print(f"{MODULE} not found under {args.reference}", file=sys.stderr)
+        return 1
+    print(out)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

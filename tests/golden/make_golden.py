@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this directory by running the REFERENCE's own
-code on CPU (run in a container where the cuda-lsr checkout is mounted):
+code on CPU (run where a cuda-lsr checkout is available):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path of the cuda-lsr checkout>
 
 * muon_golden.npz   — muon_lm_ddp.zeropower_serial / zeropower_batched_oriented /
                       MuonAdamW.muon_step (imported unmodified; the module only
@@ -12,6 +12,9 @@ code on CPU (run in a container where the cuda-lsr checkout is mounted):
                       reference source with ``ast`` and executed on CPU tensors.
 * kronrec_golden.npz — batched_kron / vectorized_kron of kron_cuda.py:117-145,
                       :618-629 on K = 5 / 4 / 3 factor sets (same extraction).
+* driver_golden.json — the key list of the run summary, the parameter count and
+                      the optimizer structure of the reference's recorded GPT-2-XL
+                      Muon run (gpt2xl_4gpu_batched.json).
 * newton_golden.npz — coupled_newton_one (+ matrix_power_small) of shampoo.py:254-347
                       (same extraction), and batched_coupled_newton (:408-542) on
                       SPD batches built as make_spd_batch (:178-247) builds them
@@ -228,10 +231,20 @@ def make_kronrec(ref: Path) -> dict:
     return out
 
 
+def make_driver(ref: Path) -> dict:
+    """The run-summary schema and GPT-2-XL optimizer structure of the reference's own recorded
+    run (gpt2xl_4gpu_batched.json, written by muon_lm_ddp.py:1539-1634): the summary's key order,
+    the model's parameter count and MuonAdamW.summary() (muon_lm_ddp.py:700-745)."""
+    import json
+    run = json.loads((ref / "gpt2xl_4gpu_batched.json").read_text())
+    return {"summary_keys": list(run.keys()), "model_params": run["model_params"],
+            "optimizer_structure": run["optimizer_structure"]}
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--only", choices=["muon", "kron", "newton", "kronrec"], default=None)
+    ap.add_argument("--reference", required=True, help="path of the cuda-lsr checkout")
+    ap.add_argument("--only", choices=["muon", "kron", "newton", "kronrec", "driver"], default=None)
     args = ap.parse_args()
     ref = Path(args.reference)
     if args.only in (None, "muon"):
@@ -242,6 +255,9 @@ def main() -> int:
         np.savez_compressed(HERE / "newton_golden.npz", **make_newton(ref))
     if args.only in (None, "kronrec"):
         np.savez_compressed(HERE / "kronrec_golden.npz", **make_kronrec(ref))
+    if args.only in (None, "driver"):
+        import json
+        (HERE / "driver_golden.json").write_text(json.dumps(make_driver(ref), indent=1) + "\n")
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
     return 0

@@ -41,6 +41,29 @@ def test_kron_sum_bf16_and_f32(shape):
     assert rel_fro(Yb.cpu().numpy(), refb) < TOL_BF16
 
 
+def test_kron_sum_1024_64rhs_workload():
+    """The Kronecker-sum workload as specified: A, B = (M + M^T)/2 with M ~ N(0, 1/1024), 1024^2,
+    drawn A then B from seed 1; X = 64 right-hand sides of 1024^2, N(0, 1), seed 2 (CPU
+    generators, the inputs bench.py times). fp32 (3xTF32) within 1e-5 of the float64 oracle;
+    bf16 within 1e-3 of the exact product of the same bf16-rounded operands."""
+    import lsr.kron as K
+    g = torch.Generator().manual_seed(1)
+    Ms = [torch.randn(1024, 1024, generator=g) / 32.0 for _ in range(2)]
+    A, B = [((m + m.T) / 2).contiguous() for m in Ms]
+    X = torch.randn(64, 1024, 1024, generator=torch.Generator().manual_seed(2))
+    Ad, Bd, Xd = A.cuda(), B.cuda(), X.cuda()
+    errs = {}
+    Y = K.kron_sum(Ad, Xd, Bd).cpu().numpy()
+    errs["fp32"] = rel_fro(Y, ok.kron_sum(X.numpy(), A.numpy(), B.numpy()))
+    del Y
+    Ab, Xb, Bb = Ad.bfloat16(), Xd.bfloat16(), Bd.bfloat16()
+    Yb = K.kron_sum(Ab, Xb, Bb).cpu().numpy()
+    errs["bf16"] = rel_fro(Yb, ok.kron_sum(Xb.float().cpu().numpy(), Ab.float().cpu().numpy(),
+                                           Bb.float().cpu().numpy()))
+    print(f"Kronecker sum 1024^2 x 64 RHS: fp32 {errs['fp32']:.2e}, bf16 {errs['bf16']:.2e}")
+    assert errs["fp32"] < TOL_F32 and errs["bf16"] < TOL_BF16, errs
+
+
 def test_kron_sum_matches_dense_operator():
     """(A ⊕ B) vec(X) against the explicitly formed A⊗I + I⊗B on a small case."""
     import lsr.kron as K

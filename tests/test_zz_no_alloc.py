@@ -3,15 +3,21 @@
 lsr_ns_bf16_noalloc exists for callers that cannot allocate device memory
 themselves (their device memory belongs to another allocator, or they cannot
 afford the synchronisation cudaMalloc/cudaFree may cause); it keeps its
-scratch in a fixed array inside the library. It must give the same results as
-lsr_ns_bf16 with a caller workspace, call after call, although every call
-reuses (and leaves behind) the same scratch contents.
+scratch in a fixed array inside the library. It runs the same kernels as
+lsr_ns_bf16 with a caller workspace, and those kernels are deterministic, so
+its output must be bit-identical to lsr_ns_bf16's, call after call, although
+every call reuses (and leaves behind) the same scratch contents; a leak of a
+previous call's scratch into a later one would break that equality. The
+result is also checked against the oracle within the Newton–Schulz tolerance.
 
 This file sorts last so that a failure here comes after every other test has
 run; it also passes when run alone in a fresh process.
 """
 import pytest
 import torch
+
+from oracle import muon as om
+from oracle.bf16 import rel_fro
 
 pytestmark = pytest.mark.gpu
 
@@ -50,7 +56,9 @@ def test_noalloc_matches_workspace_entry_point_twice():
         ref = _with_workspace(lib, L, X, rows, cols, 1)
         torch.cuda.synchronize()
         assert got.shape == ref.shape
-        assert _rel(got.float(), ref.float()) < TOL, (rows, cols)
+        assert torch.equal(got, ref), (rows, cols, _rel(got.float(), ref.float()))
+        err = rel_fro(got.float().cpu().numpy(), om.zeropower(X.float().cpu().numpy(), 5, 1e-7))
+        assert err < TOL, (rows, cols, err)
     assert L.device_status() == 0
 
 
