@@ -659,12 +659,20 @@ def run_workload(args) -> None:
                 n, r, c = grp.stack.shape
                 grp.QL, grp.QR = orth(r, n), orth(c, n)
             ms = _time_gpu(opt.step, args.warmup, args.steps)
+            from lsr import _lib
+            _lib.profile_enable(True)
+            _lib.profile_read(reset=True)
+            opt.step()
+            torch.cuda.synchronize()
+            _lib.profile_enable(False)
+            kinds = {k: round(v[0], 3) for k, v in _lib.profile_read(reset=True).items() if v[1]}
             from oracle import shampoo as osh
             fl = sum(osh.soap_flops(r, c) * len(grp.refs) for (r, c), grp, _ in opt._groups)
             lines.append({"workload": f"cfg5: GPT-2-XL SOAP step, {args.layers} layers, "
                                       f"{sum(len(grp.refs) for _, grp, _ in opt._groups)} blocks at 1024, 1 GPU",
                           "value": ms, "unit": "ms", "algorithmic_tflop": fl / 1e12, "tflops": fl / ms / 1e9,
-                          "frac_of_sustained": fl / ms / 1e9 / peaks["bf16_tflops_sustained"]})
+                          "frac_of_sustained": fl / ms / 1e9 / peaks["bf16_tflops_sustained"],
+                          "per_kind_ms_one_step": kinds})
     elif w == "kron64x8":
         # The reference's own Kronecker-sum sweep (hft_fused.py:856-862): x [M, 64, 8], S terms
         # A_s [64,64] / sqrt(64), B_s [8,8] / sqrt(8), at = A^T prepacked, fp32 (TF32 off). Its

@@ -25,15 +25,15 @@ int lsr_gemm_bf16(const void* A, const void* B, void* D, int batch, int M, int N
   Operand ob = b_trans ? Operand{B, N, K, K, (long long)N * K, batch, 0} : Operand{B, K, N, N, (long long)K * N, batch, 1};
   // Problems taller than one 128-row tile run on CTA pairs (256-row tiles, half of B per CTA).
   const bool pair = M > BM;
-  rc = make_operand_map(&p.mapA[0][0], oa, false, G_BN);
-  if (!rc) rc = make_operand_map(&p.mapB[0][0], ob, true, pair ? G_BN / 2 : G_BN);
-  if (rc) return rc;
   GroupDesc& G = p.g[0];
+  G.seg[0] = SegDesc{cdiv(K, BK), oa.mn, ob.mn, 0, 0};
+  rc = make_operand_map(&p.mapA[0][0], oa, false, G_BN, &G.seg[0].a_mn);
+  if (!rc) rc = make_operand_map(&p.mapB[0][0], ob, true, pair ? G_BN / 2 : G_BN, &G.seg[0].b_mn);
+  if (rc) return rc;
   G.batch = batch;
   G.M = M;
   G.N = N;
   G.nseg = 1;
-  G.seg[0] = SegDesc{cdiv(K, BK), oa.mn, ob.mn, 0, 0};
   G.out = D;
   G.out_bs = (long long)M * N;
   G.ldo = N;
@@ -59,15 +59,15 @@ int lsr_gram_update_f32(const void* Gm, void* S, int batch, int rows, int cols, 
   Operand o = side == 0 ? Operand{Gm, rows, cols, cols, (long long)rows * cols, batch, 0}
                         : Operand{Gm, rows, cols, cols, (long long)rows * cols, batch, 1};
   const bool pair = n > BM;
-  rc = make_operand_map(&p.mapA[0][0], o, false, G_BN);
-  if (!rc) rc = make_operand_map(&p.mapB[0][0], o, true, pair ? G_BN / 2 : G_BN);
-  if (rc) return rc;
   GroupDesc& G = p.g[0];
+  G.seg[0] = SegDesc{cdiv(side == 0 ? cols : rows, BK), o.mn, o.mn, 0, 0};
+  rc = make_operand_map(&p.mapA[0][0], o, false, G_BN, &G.seg[0].a_mn);
+  if (!rc) rc = make_operand_map(&p.mapB[0][0], o, true, pair ? G_BN / 2 : G_BN, &G.seg[0].b_mn);
+  if (rc) return rc;
   G.batch = batch;
   G.M = G.N = n;
   G.tri = 1;
   G.nseg = 1;
-  G.seg[0] = SegDesc{cdiv(side == 0 ? cols : rows, BK), o.mn, o.mn, 0, 0};
   G.out = S;
   G.out_bs = (long long)n * n;
   G.ldo = n;

@@ -69,8 +69,9 @@ __host__ __device__ __forceinline__ float tf32_hi(float x) {
 
 struct SegDesc {
   int kblocks;   // number of K blocks (64 bf16 / 32 tf32 elements each)
-  int a_mn;      // operand A stored MN-major (rows of A are columns in memory)
-  int b_mn;      // operand B stored MN-major
+  int a_mn;      // operand A stored MN-major (rows of A are columns in memory): 1 = one TMA box per
+                 // 64-element MN chunk, 2 = all chunks of the tile in one 4-D box; 0 = K-major
+  int b_mn;      // operand B likewise
   int a_bcast;   // operand A is shared by the whole batch (TMA z = 0)
   int b_bcast;
   int slot;      // dual-accumulator kernels: 0 = main products, 1 = small correction products
@@ -89,6 +90,7 @@ struct GroupDesc {
   const void* aux;
   long long aux_bs;
   int ld_aux;
+  int aux_trans;  // staged epilogues only: tile element (r, c) reads aux[c][r] (the tile is a transposed view)
   float alpha, beta;
   int tma_out;  // epilogue stages 32x32 chunks in smem and stores them with TMA (mapOut)
   void* out2;   // second output of the split epilogues (same layout as out)
@@ -361,12 +363,16 @@ __device__ __forceinline__ void aux_prefetch(const GroupDesc& G, int b, int row0
                                              uint4 (&pre)[EpiT<EPI>::VPR]) {
   using T = EpiT<EPI>;
   const uint8_t* base = reinterpret_cast<const uint8_t*>(G.aux) + (long long)b * G.aux_bs * T::ESZ;
+  // aux_trans: the 32 x 32 aux block at aux rows col0.., aux columns row0.. (staged as is,
+  // read back column-wise)
+  const int ar0 = G.aux_trans ? col0 : row0, ac0 = G.aux_trans ? row0 : col0;
+  const int arows = G.aux_trans ? G.N : G.M, acols = G.aux_trans ? G.M : G.N;
 #pragma unroll
   for (int i = 0; i < T::VPR; ++i) {
     const int idx = lane + 32 * i;
     const int r = idx / T::VPR, j = idx % T::VPR;
-    const int gr = row0 + r, gc = col0 + j * T::EPV;
-    if (gr < G.M && gc < G.N)
+    const int gr = ar0 + r, gc = ac0 + j * T::EPV;
+    if (gr < arows && gc < acols)
       pre[i] = __ldg(reinterpret_cast<const uint4*>(base + ((long long)gr * G.ld_aux + gc) * T::ESZ));
     else
       pre[i] = make_uint4(0u, 0u, 0u, 0u);
@@ -452,21 +458,30 @@ __device__ __forceinline__ void epilogue_chunk_staged(const GemmParams& p, int g
     }
     __syncwarp();
     float x[32];
+    if (!T::F32 && G.aux_trans) {
+      // column `lane` of the staged block: element (k, lane) for k < 32 (one row per step:
+      // the warp reads 64 contiguous bytes, two lanes per 32-bit word)
 #pragma unroll
-    for (int j = 0; j < T::VPR; ++j) {
-      const uint4 u = *reinterpret_cast<const uint4*>(dbuf + stg_off<T::ROWB>(lane, j));
-      if constexpr (T::F32) {
-        x[4 * j] = __uint_as_float(u.x);
-        x[4 * j + 1] = __uint_as_float(u.y);
-        x[4 * j + 2] = __uint_as_float(u.z);
-        x[4 * j + 3] = __uint_as_float(u.w);
-      } else {
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+      for (int k = 0; k < 32; ++k)
+        x[k] = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(
+            dbuf + stg_off<T::ROWB>(k, (lane * T::ESZ) / 16) + (lane * T::ESZ) % 16));
+    } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(h[e]);
-          x[8 * j + 2 * e] = f.x;
-          x[8 * j + 2 * e + 1] = f.y;
+      for (int j = 0; j < T::VPR; ++j) {
+        const uint4 u = *reinterpret_cast<const uint4*>(dbuf + stg_off<T::ROWB>(lane, j));
+        if constexpr (T::F32) {
+          x[4 * j] = __uint_as_float(u.x);
+          x[4 * j + 1] = __uint_as_float(u.y);
+          x[4 * j + 2] = __uint_as_float(u.z);
+          x[4 * j + 3] = __uint_as_float(u.w);
+        } else {
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h[e]);
+            x[8 * j + 2 * e] = f.x;
+            x[8 * j + 2 * e + 1] = f.y;
+          }
         }
       }
     }
@@ -627,10 +642,12 @@ __device__ __forceinline__ void epilogue_chunk_staged(const GemmParams& p, int g
 
 // PAIR = 1: the tile is computed by a cluster of two CTAs; each CTA holds
 // 128 rows of A and BN/2 rows of B per stage.
-template <int BN, int STAGES, int EPI, int PAIR = 0>
+// KS = 2: a stage holds two K blocks (two 128-byte swizzle atoms per K-major
+// operand row block, 2 x KE K-rows per MN-major chunk).
+template <int BN, int STAGES, int EPI, int PAIR = 0, int KS = 1>
 struct GemmSmem {
-  static constexpr int A_BYTES = BM * 128;  // 128-byte K rows, for bf16 and tf32 alike
-  static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * 128;
+  static constexpr int A_BYTES = BM * 128 * KS;  // 128-byte K rows, for bf16 and tf32 alike
+  static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * 128 * KS;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;
   static constexpr int EPI_BYTES = (kEpiThreads / 32) * 4 * EpiT<EPI>::CHB;  // per warp: 2 direct + 2 transposed
@@ -639,10 +656,13 @@ struct GemmSmem {
   static constexpr int TOTAL = BAR_OFFSET + BAR_BYTES + 1024;  // + alignment slack
 };
 
-// Pipeline depth that fits next to the epilogue staging buffers.
-template <int EPI, int PAIR = 0>
+// Pipeline depth that fits next to the epilogue staging buffers (at most 8).
+template <int EPI, int PAIR = 0, int BN = 256, int KS = 1>
 constexpr int default_stages() {
-  return PAIR ? (EpiT<EPI>::F32 ? 5 : 6) : (EpiT<EPI>::F32 ? 3 : 4);
+  using S8 = GemmSmem<BN, 8, EPI, PAIR, KS>;
+  int st = 8;
+  while (st > 2 && S8::TOTAL - (8 - st) * (S8::STAGE_BYTES + 16) > 232448) --st;
+  return st;
 }
 
 // TF32 = 0: bf16 operands (kind::f16); TF32 = 1: fp32 operands read as tf32
@@ -659,18 +679,27 @@ constexpr int default_stages() {
 // loads count on the leader's full barriers; the leader's commits arrive on
 // both CTAs' barriers; both epilogues arrive on the leader's accumulator-empty
 // barriers. No multicast is used.
-template <int BN, int STAGES, int EPI, int TF32, int DUAL, int PAIR>
+// KS = 2: each stage carries two K blocks, loaded with one 4-D TMA box per
+// operand (K-major: two 128-byte atoms; MN-major: 2 KE K-rows per chunk), so
+// the TMA operations and barrier round trips per flop halve; the MMA thread
+// issues 8 UMMAs per stage (4 when the segment's last stage holds one block).
+template <int BN, int STAGES, int EPI, int TF32, int DUAL, int PAIR, int KS = 1>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __grid_constant__ GemmParams p) {
-  static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 64 in [64, 256]");
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 32 in [64, 256]");
   constexpr int KE = TF32 ? BK_TF32 : BK;        // elements per K block (= MN elements per MN-major chunk)
-  constexpr int CHUNK = KE * 128;                // bytes of one MN-major chunk (KE K-rows of 128 B)
+  constexpr int CHUNK = KE * 128 * KS;           // bytes of one MN-major chunk (KS KE K-rows of 128 B)
   constexpr uint32_t MN_STEP = (TF32 ? 8 : 16) * 128;  // bytes between UMMA K steps, MN-major
   constexpr int ACC_COLS = DUAL ? 2 * BN : BN;          // TMEM columns per tile in flight
   constexpr int TM = PAIR ? 2 * BM : BM;                // output rows per tile
   constexpr int BNC = PAIR ? BN / 2 : BN;               // B rows loaded by this CTA
   static_assert(2 * BN <= 512, "two BN-wide accumulators must fit in TMEM");
-  static_assert(!PAIR || BNC % KE == 0, "pair B half must be whole MN-major chunks");
-  using L = GemmSmem<BN, STAGES, EPI, PAIR>;
+  static_assert(BNC % 8 == 0, "B rows per CTA must be whole 8-row swizzle groups");
+  // MN-major B needs BNC to be whole MN chunks (KE elements); launch_gemm checks it.
+  static_assert(KS == 1 || KS == 2, "a stage holds one or two K blocks");
+  static_assert(KS == 1 || !TF32, "two-block stages are bf16 only");
+  using L = GemmSmem<BN, STAGES, EPI, PAIR, KS>;
+  constexpr int A_HALF = BM * 128;   // bytes of one K block of the A tile (K-major)
+  constexpr int B_HALF = (PAIR ? BN / 2 : BN) * 128;
   using ET = EpiT<EPI>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -787,7 +816,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
           const CUtensorMap* mb = &p.mapB[g][sg];
           const int za = S.a_bcast ? 0 : b;
           const int zb = S.b_bcast ? 0 : b;
-          for (int kb = 0; kb < S.kblocks; ++kb) {
+          for (int kb = 0; kb < S.kblocks; kb += KS) {
             if (!mbar_wait(empty + s, ph ^ 1, abort_flag, p.status, ST_TIMEOUT_PRODUCER)) {
               ok = false;
               break;
@@ -795,18 +824,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
             uint8_t* sa = smem + s * L::STAGE_BYTES;
             uint8_t* sb = sa + L::A_BYTES;
             const int k0 = kb * KE;
-            if constexpr (PAIR) {
+            if constexpr (KS == 2) {
+              // one 4-D box per operand: K-major (K element, row, K block, batch) from K block kb,
+              // MN-major (MN element, K row, MN chunk, batch) over 2 KE K rows
+              if constexpr (PAIR) {
+                if (rank == 0) mbar_arrive_expect_tx(full + s, 2 * L::STAGE_BYTES);
+                const uint32_t fb = mapa_shared(smem_u32(full + s), 0);
+                if (!S.a_mn)
+                  tma_load_4d_pair(sa, ma, fb, 0, m0, kb, za);
+                else
+                  tma_load_4d_pair(sa, ma, fb, 0, k0, m0 / KE, za);
+                if (!S.b_mn)
+                  tma_load_4d_pair(sb, mb, fb, 0, n0, kb, zb);
+                else
+                  tma_load_4d_pair(sb, mb, fb, 0, k0, n0 / KE, zb);
+              } else {
+                mbar_arrive_expect_tx(full + s, L::STAGE_BYTES);
+                if (!S.a_mn)
+                  tma_load_4d(sa, ma, full + s, 0, m0, kb, za);
+                else
+                  tma_load_4d(sa, ma, full + s, 0, k0, m0 / KE, za);
+                if (!S.b_mn)
+                  tma_load_4d(sb, mb, full + s, 0, n0, kb, zb);
+                else
+                  tma_load_4d(sb, mb, full + s, 0, k0, n0 / KE, zb);
+              }
+            } else if constexpr (PAIR) {
               // the leader's full barrier counts both CTAs' bytes
               if (rank == 0) mbar_arrive_expect_tx(full + s, 2 * L::STAGE_BYTES);
               const uint32_t fb = mapa_shared(smem_u32(full + s), 0);
               if (!S.a_mn) {
                 tma_load_3d_pair(sa, ma, fb, k0, m0, za);
+              } else if (S.a_mn == 2) {
+                tma_load_4d_pair(sa, ma, fb, 0, k0, m0 / KE, za);
               } else {
 #pragma unroll
                 for (int c = 0; c < BM / KE; ++c) tma_load_3d_pair(sa + c * CHUNK, ma, fb, m0 + KE * c, k0, za);
               }
               if (!S.b_mn) {
                 tma_load_3d_pair(sb, mb, fb, k0, n0, zb);
+              } else if (S.b_mn == 2) {
+                tma_load_4d_pair(sb, mb, fb, 0, k0, n0 / KE, zb);
               } else {
 #pragma unroll
                 for (int c = 0; c < BNC / KE; ++c) tma_load_3d_pair(sb + c * CHUNK, mb, fb, n0 + KE * c, k0, zb);
@@ -815,12 +873,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
               mbar_arrive_expect_tx(full + s, L::STAGE_BYTES);
               if (!S.a_mn) {
                 tma_load_3d(sa, ma, full + s, k0, m0, za);
+              } else if (S.a_mn == 2) {
+                tma_load_4d(sa, ma, full + s, 0, k0, m0 / KE, za);
               } else {
 #pragma unroll
                 for (int c = 0; c < BM / KE; ++c) tma_load_3d(sa + c * CHUNK, ma, full + s, m0 + KE * c, k0, za);
               }
               if (!S.b_mn) {
                 tma_load_3d(sb, mb, full + s, k0, n0, zb);
+              } else if (S.b_mn == 2) {
+                tma_load_4d(sb, mb, full + s, 0, k0, n0 / KE, zb);
               } else {
 #pragma unroll
                 for (int c = 0; c < BN / KE; ++c) tma_load_3d(sb + c * CHUNK, mb, full + s, n0 + KE * c, k0, zb);
@@ -867,12 +929,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
           const uint32_t d_tmem = d_base + static_cast<uint32_t>(slot * BN);
           uint32_t accumulate = (acc_flags >> slot) & 1u;
           acc_flags |= 1u << slot;
-          const uint32_t idesc = make_idesc(TM, BN, TF32 ? 2u : 1u, (uint32_t)S.a_mn, (uint32_t)S.b_mn);
+          const uint32_t idesc = make_idesc(TM, BN, TF32 ? 2u : 1u, S.a_mn ? 1u : 0u, S.b_mn ? 1u : 0u);
           // per-UMMA descriptor advance along K, in 16-byte units: 32 B within a
           // K-major row, MN_STEP bytes (UMMA_K rows) for MN-major
           const uint32_t a_step = S.a_mn ? (MN_STEP >> 4) : (32u >> 4);
           const uint32_t b_step = S.b_mn ? (MN_STEP >> 4) : (32u >> 4);
-          for (int kb = 0; kb < S.kblocks; ++kb) {
+          for (int kb = 0; kb < S.kblocks; kb += KS) {
             if (!mbar_wait(full + s, ph, abort_flag, p.status, ST_TIMEOUT_MMA_FULL)) {
               ok = false;
               break;
@@ -882,9 +944,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
             const uint32_t sb = sa + L::A_BYTES;
             const uint64_t adesc = S.a_mn ? smem_desc_sw128(sa, CHUNK, 1024) : smem_desc_sw128(sa, 16, 1024);
             const uint64_t bdesc = S.b_mn ? smem_desc_sw128(sb, CHUNK, 1024) : smem_desc_sw128(sb, 16, 1024);
+            // UMMAs in this stage: 4 per K block present (the last stage of an odd K-block count
+            // holds one block; its second half is zero-filled and skipped)
+            const int nk = (KS == 2 && kb + 1 >= S.kblocks) ? 4 : 4 * KS;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint64_t ad = adesc + (uint64_t)(k * a_step), bd = bdesc + (uint64_t)(k * b_step);
+            for (int k = 0; k < 4 * KS; ++k) {
+              if (k >= nk) break;
+              // K-major: the second K block's atom follows the first (A_HALF / B_HALF bytes on);
+              // MN-major: K rows continue within each chunk
+              const uint32_t a_off = S.a_mn ? (uint32_t)(k * a_step) : (uint32_t)((k >> 2) * (A_HALF >> 4) + (k & 3) * a_step);
+              const uint32_t b_off = S.b_mn ? (uint32_t)(k * b_step) : (uint32_t)((k >> 2) * (B_HALF >> 4) + (k & 3) * b_step);
+              const uint64_t ad = adesc + (uint64_t)a_off, bd = bdesc + (uint64_t)b_off;
               if constexpr (PAIR) {
                 if constexpr (TF32)
                   umma_tf32_pair(d_tmem, ad, bd, idesc, accumulate);

@@ -160,14 +160,14 @@ int lsr_kron_sum_bf16(const void* A, const void* X, const void* B, float* Y, int
   G.N = n;
   G.nseg = 2;
   // segment 0: A (K-major, shared) x X (MN-major): sum_k A[r][k] X[k][c]
+  G.seg[0] = SegDesc{cdiv(m, BK), 0, 1, 1, 0};
+  G.seg[1] = SegDesc{cdiv(n, BK), 0, 0, 0, 1};
   rc = make_operand_map(&p.mapA[0][0], mat(A, m, m, 1, 0, 0), false, K_BN);
-  if (!rc) rc = make_operand_map(&p.mapB[0][0], mat(X, m, n, batch, 1, 0), true, K_BN);
+  if (!rc) rc = make_operand_map(&p.mapB[0][0], mat(X, m, n, batch, 1, 0), true, K_BN, &G.seg[0].b_mn);
   // segment 1: X (K-major) x B (K-major, shared): sum_k X[r][k] B[c][k]
   if (!rc) rc = make_operand_map(&p.mapA[0][1], mat(X, m, n, batch, 0, 0), false, K_BN);
   if (!rc) rc = make_operand_map(&p.mapB[0][1], mat(B, n, n, 1, 0, 0), true, K_BN);
   if (rc) return rc;
-  G.seg[0] = SegDesc{cdiv(m, BK), 0, 1, 1, 0};
-  G.seg[1] = SegDesc{cdiv(n, BK), 0, 0, 0, 1};
   G.out = Y;
   G.out_bs = (long long)m * n;
   G.ldo = n;
@@ -250,9 +250,9 @@ namespace {
 int set_segments(GemmParams& p, const Operand (*pairs)[2], const SegDesc* segs, int nseg) {
   int rc = 0;
   for (int t = 0; t < nseg && !rc; ++t) {
-    rc = make_operand_map(&p.mapA[0][t], pairs[t][0], false, K_BN);
-    if (!rc) rc = make_operand_map(&p.mapB[0][t], pairs[t][1], true, K_BN);
     p.g[0].seg[t] = segs[t];
+    rc = make_operand_map(&p.mapA[0][t], pairs[t][0], false, K_BN, &p.g[0].seg[t].a_mn);
+    if (!rc) rc = make_operand_map(&p.mapB[0][t], pairs[t][1], true, K_BN, &p.g[0].seg[t].b_mn);
   }
   p.g[0].nseg = nseg;
   return rc;
@@ -384,24 +384,20 @@ int kron_term_f32(const float* Ah, const float* Al, const float* Xh, const float
   return rc ? rc : launch_gemm<K_BN, EPI_F32_EMA, default_stages<EPI_F32_EMA>(), 1, 1>(p, st);
 }
 
-// Dense small-factor path (see kron_use_dense): W pair, X pair, one 3xTF32 GEMM.
-int kron_apply_dense_f32(const void* A, int a_trans, const void* X, const void* B, float* Y, int batch, int m, int n,
-                         int nterms, uint8_t* w, cudaStream_t st) {
-  const int mn = m * n;
-  const size_t wbytes = (size_t)mn * mn * 4, xbytes = (size_t)batch * mn * 4;
-  float* Wh = reinterpret_cast<float*>(w);
-  float* Wl = reinterpret_cast<float*>(w + a256(wbytes));
-  float* Xh = reinterpret_cast<float*>(w + 2 * a256(wbytes));
-  float* Xl = reinterpret_cast<float*>(w + 2 * a256(wbytes) + a256(xbytes));
-  {
-    const long long total = (long long)mn * mn;
-    const int blocks = (int)std::min<long long>((total + SPLIT_THREADS - 1) / SPLIT_THREADS, 148LL * 16);
-    ProfScope prof(PK_EW_OTHER, st);
-    kron_dense_w_kernel<<<blocks, SPLIT_THREADS, 0, st>>>(static_cast<const float*>(A), a_trans,
-                                                          static_cast<const float*>(B), m, n, nterms, Wh, Wl);
-    if (launch_ok()) return LSR_ERR_LAUNCH;
-  }
-  int rc = split_tf32(static_cast<const float*>(X), Xh, Xl, (long long)batch * mn, st);
+// Dense small-factor path (see kron_use_dense): the operator's tf32 pair W = Wh + Wl ...
+int dense_operator(const float* A, int a_trans, const float* B, int m, int n, int nterms, float* Wh, float* Wl,
+                   cudaStream_t st) {
+  const long long mn = (long long)m * n, total = mn * mn;
+  const int blocks = (int)std::min<long long>((total + SPLIT_THREADS - 1) / SPLIT_THREADS, 148LL * 16);
+  ProfScope prof(PK_EW_OTHER, st);
+  kron_dense_w_kernel<<<blocks, SPLIT_THREADS, 0, st>>>(A, a_trans, B, m, n, nterms, Wh, Wl);
+  return launch_ok();
+}
+
+// ... and Y_flat = X_flat W^T: the X pair, one 3xTF32 GEMM (rows = batch, K = N = mn).
+int dense_apply(const float* Wh, const float* Wl, const float* X, float* Y, int batch, int mn, float* Xh, float* Xl,
+                cudaStream_t st) {
+  int rc = split_tf32(X, Xh, Xl, (long long)batch * mn, st);
   if (rc) return rc;
   GemmParams p{};
   p.ngroups = 1;
@@ -415,6 +411,18 @@ int kron_apply_dense_f32(const void* A, int a_trans, const void* X, const void* 
   const SegDesc sg[3] = {sd, sc, sc};
   rc = set_segments(p, pr, sg, 3);
   return rc ? rc : launch_gemm<K_BN, EPI_STORE_F32, default_stages<EPI_STORE_F32>(), 1, 1>(p, st);
+}
+
+int kron_apply_dense_f32(const void* A, int a_trans, const void* X, const void* B, float* Y, int batch, int m, int n,
+                         int nterms, uint8_t* w, cudaStream_t st) {
+  const int mn = m * n;
+  const size_t wbytes = (size_t)mn * mn * 4, xbytes = (size_t)batch * mn * 4;
+  float* Wh = reinterpret_cast<float*>(w);
+  float* Wl = reinterpret_cast<float*>(w + a256(wbytes));
+  float* Xh = reinterpret_cast<float*>(w + 2 * a256(wbytes));
+  float* Xl = reinterpret_cast<float*>(w + 2 * a256(wbytes) + a256(xbytes));
+  int rc = dense_operator(static_cast<const float*>(A), a_trans, static_cast<const float*>(B), m, n, nterms, Wh, Wl, st);
+  return rc ? rc : dense_apply(Wh, Wl, static_cast<const float*>(X), Y, batch, mn, Xh, Xl, st);
 }
 
 int kron_apply(const void* A, int a_trans, const void* X, const void* B, float* Y, int batch, int m, int n,
@@ -502,6 +510,34 @@ int lsr_gemm_f32(const float* A, const float* B, float* C, int batch, int M, int
   const SegDesc sg[3] = {sd, sc, sc};
   rc = set_segments(p, pr, sg, 3);
   return rc ? rc : launch_gemm<K_BN, EPI_STORE_F32, default_stages<EPI_STORE_F32>(), 1, 1>(p, st);
+}
+
+int lsr_kron_dense_operator_f32(const float* A, int a_trans, const float* B, int m, int n, int nterms, float* Wh,
+                                float* Wl, lsr_stream_t stream) {
+  if (!kron_dims_ok(1, m, n, nterms) || (long long)m * n > kDenseMaxMN) return LSR_ERR_ARG;
+  if (!A || !B || !Wh || !Wl) return LSR_ERR_ARG;
+  int rc = check_device();
+  if (rc) return rc;
+  return dense_operator(A, a_trans, B, m, n, nterms, Wh, Wl, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t lsr_kron_dense_apply_workspace_bytes(int batch, int mn) {
+  if (batch < 0 || mn <= 0) return 0;
+  return 2 * a256((size_t)std::max(batch, 1) * mn * 4) + 256;
+}
+
+int lsr_kron_dense_apply_f32(const float* Wh, const float* Wl, const float* X, float* Y, int batch, int mn, void* ws,
+                             size_t ws_bytes, lsr_stream_t stream) {
+  if (batch < 0 || mn <= 0 || mn > kDenseMaxMN || mn % 4) return LSR_ERR_ARG;
+  if (batch == 0) return LSR_OK;
+  if (!Wh || !Wl || !X || !Y) return LSR_ERR_ARG;
+  int rc = check_device();
+  if (rc) return rc;
+  if (!ws || ws_bytes < lsr_kron_dense_apply_workspace_bytes(batch, mn)) return LSR_ERR_WORKSPACE;
+  uint8_t* w = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(ws), 256));
+  float* Xh = reinterpret_cast<float*>(w);
+  float* Xl = reinterpret_cast<float*>(w + a256((size_t)batch * mn * 4));
+  return dense_apply(Wh, Wl, X, Y, batch, mn, Xh, Xl, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int lsr_kron_apply_bf16(const void* A, int a_trans, const void* X, const void* B, float* Y, int batch, int m, int n,

@@ -692,23 +692,61 @@ int run_prologue(NsGroup* gs, const ProSource* srcs, int ng, const Control& ctl,
 }
 
 // `steps` quintic iterations over up to kMaxGroups groups.
-template <int EPI>
+template <int EPI, int BN = NS_BN, int KS = 1>
 int launch_ns(GemmParams& p, cudaStream_t st, int kind, bool pair) {
-  if (pair) return launch_gemm<NS_BN, EPI, default_stages<EPI, 1>(), 0, 0, 1>(p, st, kind);
-  return launch_gemm<NS_BN, EPI>(p, st, kind);
+  if (pair) return launch_gemm<BN, EPI, default_stages<EPI, 1, BN, KS>(), 0, 0, 1, KS>(p, st, kind);
+  return launch_gemm<BN, EPI, default_stages<EPI, 0, BN, KS>(), 0, 0, 0, KS>(p, st, kind);
+}
+
+// The update runs two K blocks (128 elements) per pipeline stage when its K
+// length (m) and the MN-major rows of X (n) are whole numbers of 64-element
+// blocks: half the TMA operations and barrier round trips per flop (GPT-2-XL
+// step: 23.5 vs 25.4 ms per step). The symmetric products keep one block per
+// stage: their single-CTA tiles fit only two double-width stages, and lost more
+// to the shallower pipeline than they gained (X X^T 14.9 vs 13.3 ms).
+bool ns_use_ks2(const NsGroup* gs, int ng) {
+  for (int g = 0; g < ng; ++g)
+    if (gs[g].m % BK || gs[g].n % BK) return false;
+  return ng > 0;
+}
+
+// Narrow tiles: when every group's oriented row count m is a multiple of
+// NS_BN_NARROW but not of the 256-row pair tile (GPT-2-XL: m = 1600 = 10 x 160 =
+// 6.25 x 256), the m-wide dimension of every product is tiled exactly:
+//   * X X^T and A A (m x m, single CTAs): 128 x 160 tiles, no padded columns;
+//   * the update runs transposed, X'^T = X^T B (B is symmetric): the n x m
+//     output in 256 x 160 pair tiles, X^T read MN-major, the a X term read
+//     transposed by the epilogue and the tile stored transposed.
+// Otherwise 128 x 256 / 256 x 256 tiles with the update in its own orientation.
+constexpr int NS_BN_NARROW = 160;
+
+constexpr bool kNsNarrowTiles = false;
+
+bool ns_use_narrow(const NsGroup* gs, int ng) {
+  if (!kNsNarrowTiles) return false;
+  for (int g = 0; g < ng; ++g) {
+    const NsGroup& S = gs[g];
+    if (S.m % NS_BN_NARROW != 0 || S.m % (2 * BM) == 0) return false;
+    // the transposed update needs the staged (TMA) epilogue for its output
+    if (S.final_out && ((reinterpret_cast<uintptr_t>(S.final_out) & 15) || S.final_ld % 8 || S.final_bs % 8))
+      return false;
+  }
+  return ng > 0;
 }
 
 int ns_iterations(NsGroup* gs, int ng, int steps, float a, float b, float c, cudaStream_t st) {
-  constexpr int BN = NS_BN;
-  // The update X' = a X + B X of matrices taller than one 128-row tile runs on
-  // CTA pairs: 256-row tiles, each CTA loading half of operand B, so the
-  // tensor cores need a third less operand bandwidth per flop. The symmetric
-  // products (X X^T and A A, upper-triangle tiles) run on single CTAs: their
-  // 128-row tiles pad a 1600-row output to 1664 rows instead of 1792 (measured
-  // on the GPT-2-XL step: X X^T 12.4 vs 13.4 ms, b A + c A^2 4.9 vs 5.4 ms per
-  // step, while the paired update is 1.6 ms faster than single-CTA tiles).
+  const bool narrow = ns_use_narrow(gs, ng);
+  const int BN = narrow ? NS_BN_NARROW : NS_BN;
+  const int ks = (!narrow && ns_use_ks2(gs, ng)) ? 2 : 1;
+  // The update of matrices taller than one 128-row tile runs on CTA pairs:
+  // 256-row tiles, each CTA loading half of operand B, so the tensor cores need
+  // a third less operand bandwidth per flop. The symmetric products (X X^T and
+  // A A, upper-triangle tiles) run on single CTAs: 128-row tiles pad a 1600-row
+  // output to 1664 rows instead of 1792 (measured on the GPT-2-XL step with
+  // 256-wide tiles: X X^T 12.4 vs 13.4 ms, b A + c A^2 4.9 vs 5.4 ms per step,
+  // while the paired update is 1.6 ms faster than single-CTA tiles).
   bool pair = false;
-  for (int g = 0; g < ng; ++g) pair |= gs[g].m > BM;
+  for (int g = 0; g < ng; ++g) pair |= (narrow ? gs[g].n : gs[g].m) > BM;
   const int BB = pair ? BN / 2 : BN;  // operand-B box rows of the update
   for (int it = 0; it < steps; ++it) {
     const int cur = it & 1, nxt = cur ^ 1;
@@ -750,37 +788,62 @@ int ns_iterations(NsGroup* gs, int ng, int steps, float a, float b, float c, cud
       G2.ld_aux = S.ldm;
       G2.alpha = b;
       G2.beta = c;
-      // phase 3: X' = a X + B X   (X is the MN-major B operand)
-      Operand bk{S.B, S.m, S.m, S.ldm, abs_, S.batch, 0};
-      Operand xmn{S.X[cur], S.m, S.n, S.ldn, xbs, S.batch, 1};
-      if (!rc) rc = make_operand_map(&p3.mapA[g][0], bk, false, BN);
-      if (!rc) rc = make_operand_map(&p3.mapB[g][0], xmn, true, BB);
-      if (rc) return rc;
+      // phase 3: X' = a X + B X
       GroupDesc& G3 = p3.g[g];
       G3.batch = S.batch;
-      G3.M = S.m;
-      G3.N = S.n;
       G3.tri = 0;
       G3.nseg = 1;
-      G3.seg[0] = SegDesc{cdiv(S.m, BK), 0, 1, 0, 0};
       G3.aux = S.X[cur];
       G3.aux_bs = xbs;
       G3.ld_aux = S.ldn;
       G3.alpha = a;
-      if (last && S.final_out) {
+      Operand bk{S.B, S.m, S.m, S.ldm, abs_, S.batch, 0};
+      Operand xmn{S.X[cur], S.m, S.n, S.ldn, xbs, S.batch, 1};
+      const bool to_final = last && S.final_out;
+      if (!narrow) {
+        // X' (m x n) = B X: B K-major, X the MN-major B operand
+        G3.seg[0] = SegDesc{cdiv(S.m, BK), 0, 1, 0, 0};
+        if (!rc) rc = make_operand_map(&p3.mapA[g][0], bk, false, BN, nullptr, ks);
+        if (!rc) rc = make_operand_map(&p3.mapB[g][0], xmn, true, BB, &G3.seg[0].b_mn, ks);
+        G3.M = S.m;
+        G3.N = S.n;
+        G3.out_trans = to_final ? S.final_trans : 0;
+      } else {
+        // X'^T (n x m) = X^T B: X^T the MN-major A operand, B (symmetric) K-major;
+        // the tile's (j, i) element is X'[i][j]
+        G3.seg[0] = SegDesc{cdiv(S.m, BK), 1, 0, 0, 0};
+        if (!rc) rc = make_operand_map(&p3.mapA[g][0], xmn, false, BN, &G3.seg[0].a_mn);
+        if (!rc) rc = make_operand_map(&p3.mapB[g][0], bk, true, BB);
+        G3.M = S.n;
+        G3.N = S.m;
+        G3.aux_trans = 1;
+        G3.out_trans = to_final ? !S.final_trans : 1;
+      }
+      if (rc) return rc;
+      if (to_final) {
         G3.out = S.final_out;
         G3.out_bs = S.final_bs;
         G3.ldo = S.final_ld;
-        G3.out_trans = S.final_trans;
       } else {
         G3.out = S.X[nxt];
         G3.out_bs = xbs;
         G3.ldo = S.ldn;
       }
     }
-    int rc = launch_ns<EPI_NS_GRAM>(p1, st, PK_GEMM_GRAM, false);
-    if (!rc) rc = launch_ns<EPI_NS_POLY>(p2, st, PK_GEMM_POLY, false);
-    if (!rc) rc = launch_ns<EPI_NS_UPDATE>(p3, st, PK_GEMM_UPDATE, pair);
+    int rc;
+    if (narrow) {
+      rc = launch_ns<EPI_NS_GRAM, NS_BN_NARROW>(p1, st, PK_GEMM_GRAM, false);
+      if (!rc) rc = launch_ns<EPI_NS_POLY, NS_BN_NARROW>(p2, st, PK_GEMM_POLY, false);
+      if (!rc) rc = launch_ns<EPI_NS_UPDATE, NS_BN_NARROW>(p3, st, PK_GEMM_UPDATE, pair);
+    } else if (ks == 2) {
+      rc = launch_ns<EPI_NS_GRAM>(p1, st, PK_GEMM_GRAM, false);
+      if (!rc) rc = launch_ns<EPI_NS_POLY>(p2, st, PK_GEMM_POLY, false);
+      if (!rc) rc = launch_ns<EPI_NS_UPDATE, NS_BN, 2>(p3, st, PK_GEMM_UPDATE, pair);
+    } else {
+      rc = launch_ns<EPI_NS_GRAM>(p1, st, PK_GEMM_GRAM, false);
+      if (!rc) rc = launch_ns<EPI_NS_POLY>(p2, st, PK_GEMM_POLY, false);
+      if (!rc) rc = launch_ns<EPI_NS_UPDATE>(p3, st, PK_GEMM_UPDATE, pair);
+    }
     if (rc) return rc;
   }
   return LSR_OK;

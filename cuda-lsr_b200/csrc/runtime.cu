@@ -140,6 +140,59 @@ int check_device() {
   return major == 10 ? LSR_OK : LSR_ERR_DEVICE;
 }
 
+namespace {
+EncodeTiledFn encode_fn() {
+  EncodeTiledFn encode = g_encode.load(std::memory_order_relaxed);
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return nullptr;
+    encode = reinterpret_cast<EncodeTiledFn>(fn);
+    g_encode.store(encode, std::memory_order_relaxed);
+  }
+  return encode;
+}
+}  // namespace
+
+int encode_tmap_k_blocks(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                         uint64_t block, uint64_t rows, uint64_t nblocks, uint64_t batch, uint64_t ld,
+                         uint64_t bstride, uint32_t box_rows, uint32_t box_blocks) {
+  EncodeTiledFn encode = encode_fn();
+  if (!encode) return LSR_ERR_DRIVER;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * elem_bytes) & 15) || ((bstride * elem_bytes) & 15) ||
+      ((block * elem_bytes) & 15))
+    return LSR_ERR_SHAPE;
+  // dims: element within a K block (contiguous), row, K block, batch
+  cuuint64_t dims[4] = {block, rows, nblocks, batch};
+  cuuint64_t strides[3] = {ld * elem_bytes, block * elem_bytes, bstride * elem_bytes};
+  cuuint32_t box[4] = {(cuuint32_t)block, box_rows, box_blocks, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode(map, dtype, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LSR_OK : LSR_ERR_DRIVER;
+}
+
+int encode_tmap_mn_chunks(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                          uint64_t chunk, uint64_t krows, uint64_t nchunks, uint64_t batch, uint64_t ld,
+                          uint64_t bstride, uint32_t box_chunks, uint32_t box_krows) {
+  EncodeTiledFn encode = encode_fn();
+  if (!encode) return LSR_ERR_DRIVER;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * elem_bytes) & 15) || ((bstride * elem_bytes) & 15) ||
+      ((chunk * elem_bytes) & 15))
+    return LSR_ERR_SHAPE;
+  // dims: element within a chunk (contiguous), K row, chunk, batch
+  cuuint64_t dims[4] = {chunk, krows, nchunks, batch};
+  cuuint64_t strides[3] = {ld * elem_bytes, chunk * elem_bytes, bstride * elem_bytes};
+  cuuint32_t box[4] = {(cuuint32_t)chunk, box_krows, box_chunks, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode(map, dtype, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LSR_OK : LSR_ERR_DRIVER;
+}
+
 int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t inner,
                    uint64_t outer, uint64_t batch, uint64_t ld, uint64_t bstride, uint32_t box_inner,
                    uint32_t box_outer, CUtensorMapSwizzle swizzle) {

@@ -72,14 +72,53 @@ struct Operand {
   int f32 = 0;  // fp32 storage read as tf32 (else bf16)
 };
 
+// [batch][K rows][nchunks][chunk] view of a row-major MN-major operand whose row length is a
+// whole number of 128-byte chunks: one TMA box then carries all of a tile's chunks.
+int encode_tmap_mn_chunks(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                          uint64_t chunk, uint64_t krows, uint64_t nchunks, uint64_t batch, uint64_t ld,
+                          uint64_t bstride, uint32_t box_chunks, uint32_t box_krows);
+// [batch][K blocks][rows][block] view of a K-major operand whose K length is a
+// whole number of 128-byte blocks: one TMA box carries two K blocks of a tile.
+int encode_tmap_k_blocks(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                         uint64_t block, uint64_t rows, uint64_t nblocks, uint64_t batch, uint64_t ld,
+                         uint64_t bstride, uint32_t box_rows, uint32_t box_blocks);
+
 // Tensor map for operand A (is_b = false, box rows BM) or B (box rows BN):
-// K-major box = one 128-byte K row x rows; MN-major box = 128 bytes of MN x one K block.
-inline int make_operand_map(CUtensorMap* map, const Operand& o, bool is_b, int BN) {
+// K-major box = one 128-byte K row x rows; MN-major box = 128 bytes of MN x one K
+// block, or, when the MN length is a whole number of 128-byte chunks, all of the
+// tile's MN chunks in one 4-D box (one TMA operation instead of one per chunk).
+// *mode receives the operand's load mode for SegDesc::a_mn / b_mn:
+// 0 K-major, 1 MN-major chunk boxes, 2 MN-major single 4-D box.
+// ks = 2 (two K blocks per pipeline stage): K-major operands need a K length of
+// whole blocks, MN-major ones whole MN chunks; both become single 4-D boxes
+// (LSR_ERR_SHAPE otherwise, and the caller keeps ks = 1).
+inline int make_operand_map(CUtensorMap* map, const Operand& o, bool is_b, int BN, int* mode = nullptr, int ks = 1) {
   const uint32_t ke = o.f32 ? BK_TF32 : BK;
-  const uint32_t box_outer = o.mn ? ke : static_cast<uint32_t>(is_b ? BN : BM);
-  return encode_tmap_3d(map, o.f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                        o.f32 ? 4 : 2, o.base, (uint64_t)o.cols, (uint64_t)o.rows, (uint64_t)std::max(o.batch, 1),
-                        (uint64_t)o.ld, (uint64_t)std::max<long long>(o.bs, (long long)o.rows * o.ld), ke, box_outer);
+  const CUtensorMapDataType dt = o.f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int esz = o.f32 ? 4 : 2;
+  const uint64_t bs = (uint64_t)std::max<long long>(o.bs, (long long)o.rows * o.ld);
+  const int box_rows = is_b ? BN : BM;
+  if (ks == 2) {
+    if (o.f32 || o.cols % (int)ke) return LSR_ERR_SHAPE;
+    if (mode) *mode = o.mn ? 2 : 0;
+    if (!o.mn)
+      return encode_tmap_k_blocks(map, dt, esz, o.base, ke, (uint64_t)o.rows, (uint64_t)(o.cols / ke),
+                                  (uint64_t)std::max(o.batch, 1), (uint64_t)o.ld, bs, (uint32_t)box_rows, 2u);
+    if (box_rows % (int)ke) return LSR_ERR_SHAPE;
+    return encode_tmap_mn_chunks(map, dt, esz, o.base, ke, (uint64_t)o.rows, (uint64_t)(o.cols / ke),
+                                 (uint64_t)std::max(o.batch, 1), (uint64_t)o.ld, bs, (uint32_t)(box_rows / ke), 2 * ke);
+  }
+  if (o.mn && o.cols % (int)ke == 0 && box_rows % (int)ke == 0 &&
+      encode_tmap_mn_chunks(map, dt, esz, o.base, ke, (uint64_t)o.rows, (uint64_t)(o.cols / ke),
+                            (uint64_t)std::max(o.batch, 1), (uint64_t)o.ld, bs, (uint32_t)(box_rows / ke),
+                            ke) == LSR_OK) {
+    if (mode) *mode = 2;
+    return LSR_OK;
+  }
+  if (mode) *mode = o.mn ? 1 : 0;
+  const uint32_t box_outer = o.mn ? ke : static_cast<uint32_t>(box_rows);
+  return encode_tmap_3d(map, dt, esz, o.base, (uint64_t)o.cols, (uint64_t)o.rows, (uint64_t)std::max(o.batch, 1),
+                        (uint64_t)o.ld, bs, ke, box_outer);
 }
 
 // Fill tile counts and the flat tile numbering of every group (tiles of TM x BN).
@@ -141,18 +180,30 @@ inline void setup_out_map(GemmParams& p, int g) {
 
 // Launch the engine. PAIR = 1 launches clusters of two CTAs (256-row tiles;
 // the caller builds operand-B tensor maps with BN / 2-row boxes).
-template <int BN, int EPI, int STAGES = default_stages<EPI>(), int TF32 = 0, int DUAL = 0, int PAIR = 0>
+template <int BN, int EPI, int STAGES = default_stages<EPI>(), int TF32 = 0, int DUAL = 0, int PAIR = 0, int KS = 1>
 inline int launch_gemm(GemmParams& p, cudaStream_t st, int kind = PK_GEMM_OTHER) {
-  using L = GemmSmem<BN, STAGES, EPI, PAIR>;
+  using L = GemmSmem<BN, STAGES, EPI, PAIR, KS>;
   static_assert(L::TOTAL <= 232448, "shared memory budget exceeded");
   constexpr int TM = PAIR ? 2 * BM : BM;
   finalize_tiles<BN, TM>(p);
   if (p.total_tiles == 0) return LSR_OK;
-  for (int g = 0; g < p.ngroups; ++g) setup_out_map<EPI>(p, g);
+  for (int g = 0; g < p.ngroups; ++g) {
+    setup_out_map<EPI>(p, g);
+    const GroupDesc& G = p.g[g];
+    // a transposed aux read exists only in the staged bf16 epilogue
+    if (G.aux_trans && (!G.tma_out || EpiT<EPI>::F32)) return LSR_ERR_SHAPE;
+    // MN-major operands are loaded as whole chunks of one 128-byte row of MN elements
+    constexpr int KE = TF32 ? BK_TF32 : BK;
+    for (int sg = 0; sg < G.nseg; ++sg) {
+      if (G.seg[sg].b_mn && ((PAIR ? BN / 2 : BN) % KE)) return LSR_ERR_SHAPE;
+      // two-block stages load MN-major operands as single 4-D boxes only
+      if (KS == 2 && (G.seg[sg].a_mn == 1 || G.seg[sg].b_mn == 1)) return LSR_ERR_SHAPE;
+    }
+  }
   p.status = status_ptr();
   p.sched = sched_slot();
   if (!p.status || !p.sched) return LSR_ERR_LAUNCH;
-  auto kfn = gemm_sm100_kernel<BN, STAGES, EPI, TF32, DUAL, PAIR>;
+  auto kfn = gemm_sm100_kernel<BN, STAGES, EPI, TF32, DUAL, PAIR, KS>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL) != cudaSuccess)
     return LSR_ERR_LAUNCH;
   ProfScope prof(kind, st);

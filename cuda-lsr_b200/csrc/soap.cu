@@ -40,9 +40,9 @@ Operand bmat(const void* base, int rows, int cols, int batch, int mn) {
 int set_pairs(GemmParams& p, const Operand (*pairs)[2], int nseg, int kblocks) {
   int rc = 0;
   for (int t = 0; t < nseg && !rc; ++t) {
-    rc = make_operand_map(&p.mapA[0][t], pairs[t][0], false, S_BN);
-    if (!rc) rc = make_operand_map(&p.mapB[0][t], pairs[t][1], true, S_BN);
     p.g[0].seg[t] = SegDesc{kblocks, pairs[t][0].mn, pairs[t][1].mn, 0, 0, 0};
+    rc = make_operand_map(&p.mapA[0][t], pairs[t][0], false, S_BN, &p.g[0].seg[t].a_mn);
+    if (!rc) rc = make_operand_map(&p.mapB[0][t], pairs[t][1], true, S_BN, &p.g[0].seg[t].b_mn);
   }
   p.g[0].nseg = nseg;
   return rc;
@@ -68,11 +68,27 @@ int stats_update(const void* G, float* L, float* R, int batch, int r, int c, flo
   return rc;
 }
 
-__global__ void blocks_gather_kernel(const uint64_t* ptrs, const int* lds, int rows, int cols, bf16* stack) {
+// Parameter blocks move as 16-byte vectors (8 bf16) when the block row length
+// (checked on the host) and the block's row stride and addresses (checked per
+// block on the device) allow it; otherwise element by element. One thread per
+// vector of one row; blockIdx.y = block.
+__device__ __forceinline__ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+__global__ void blocks_gather_kernel(const uint64_t* ptrs, const int* lds, int rows, int cols, bf16* stack, int vec) {
   const int b = blockIdx.y;
   const bf16* src = reinterpret_cast<const bf16*>(ptrs[b]);
   const int ld = lds[b];
   bf16* dst = stack + (long long)b * rows * cols;
+  if (vec && ld % 8 == 0 && al16(src) && al16(dst)) {
+    const int vpr = cols / 8;
+    const long long nv = (long long)rows * vpr;
+    for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (long long)gridDim.x * blockDim.x) {
+      const int r = (int)(v / vpr), c = (int)(v % vpr) * 8;
+      *reinterpret_cast<uint4*>(dst + (long long)r * cols + c) =
+          __ldcs(reinterpret_cast<const uint4*>(src + (long long)r * ld + c));
+    }
+    return;
+  }
   const long long n = (long long)rows * cols;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const int r = (int)(i / cols), c = (int)(i % cols);
@@ -83,14 +99,62 @@ __global__ void blocks_gather_kernel(const uint64_t* ptrs, const int* lds, int r
 // p = bf16(p * (1 - lr*wd)); p = bf16(p - lr * U)  on each block (decoupled weight decay).
 // U is fp32, bf16 or fp16 (the ZeRO-1 exchange's communication dtype); block b
 // reads U entry uidx[b] (b when uidx is null).
+__device__ __forceinline__ void load8(const float* u, float (&f)[8]) {
+  const float4 a = __ldcs(reinterpret_cast<const float4*>(u)), c = __ldcs(reinterpret_cast<const float4*>(u) + 1);
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = c.x; f[5] = c.y; f[6] = c.z; f[7] = c.w;
+}
+__device__ __forceinline__ void load8(const bf16* u, float (&f)[8]) {
+  const uint4 v = __ldcs(reinterpret_cast<const uint4*>(u));
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 t = __bfloat1622float2(h[e]);
+    f[2 * e] = t.x;
+    f[2 * e + 1] = t.y;
+  }
+}
+__device__ __forceinline__ void load8(const __half* u, float (&f)[8]) {
+  const uint4 v = __ldcs(reinterpret_cast<const uint4*>(u));
+  const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 t = __half22float2(h[e]);
+    f[2 * e] = t.x;
+    f[2 * e + 1] = t.y;
+  }
+}
+
 template <typename UT>
 __global__ void blocks_apply_kernel(const uint64_t* ptrs, const int* lds, int rows, int cols, const UT* U,
-                                    const int* uidx, float wd_factor, int apply_wd, float neg_lr) {
+                                    const int* uidx, float wd_factor, int apply_wd, float neg_lr, int vec) {
   const int b = blockIdx.y;
   bf16* dst = reinterpret_cast<bf16*>(ptrs[b]);
   const int ld = lds[b];
   const long long n = (long long)rows * cols;
   const UT* u = U + (long long)(uidx ? uidx[b] : b) * n;
+  if (vec && ld % 8 == 0 && al16(dst) && al16(u)) {
+    const int vpr = cols / 8;
+    const long long nv = (long long)rows * vpr;
+    for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (long long)gridDim.x * blockDim.x) {
+      const int r = (int)(v / vpr), c = (int)(v % vpr) * 8;
+      float uf[8];
+      load8(u + (long long)r * cols + c, uf);
+      uint4* q = reinterpret_cast<uint4*>(dst + (long long)r * ld + c);
+      uint4 pv = *q;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 t = __bfloat1622float2(h[e]);
+        if (apply_wd) {
+          t.x = bf16r(t.x * wd_factor);
+          t.y = bf16r(t.y * wd_factor);
+        }
+        h[e] = __floats2bfloat162_rn(fmaf(neg_lr, uf[2 * e], t.x), fmaf(neg_lr, uf[2 * e + 1], t.y));
+      }
+      *q = pv;
+    }
+    return;
+  }
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const int r = (int)(i / cols), c = (int)(i % cols);
     bf16* q = dst + (long long)r * ld + c;
@@ -330,9 +394,12 @@ int lsr_blocks_gather_bf16(const uint64_t* ptrs, const int* lds, int nblocks, in
   int rc = check_device();
   if (rc) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int blocks = (int)std::min<long long>(((long long)rows * cols + 255) / 256, 1024);
+  const int vec = cols % 8 == 0;  // row strides and addresses are checked per block on the device
+  const long long work = (long long)rows * (vec ? cols / 8 : cols);
+  const int blocks = (int)std::max<long long>(1, std::min<long long>((work + 255) / 256, 1024));
   ProfScope prof(PK_EW_OTHER, st);
-  blocks_gather_kernel<<<dim3(blocks, nblocks), 256, 0, st>>>(ptrs, lds, rows, cols, reinterpret_cast<bf16*>(stack));
+  blocks_gather_kernel<<<dim3(blocks, nblocks), 256, 0, st>>>(ptrs, lds, rows, cols, reinterpret_cast<bf16*>(stack),
+                                                              vec);
   return cudaGetLastError() == cudaSuccess ? LSR_OK : LSR_ERR_LAUNCH;
 }
 
@@ -350,19 +417,21 @@ int lsr_blocks_apply_any(const uint64_t* ptrs, const int* lds, int nblocks, int 
   int rc = check_device();
   if (rc) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int blocks = (int)std::min<long long>(((long long)rows * cols + 255) / 256, 1024);
+  const int vec = cols % 8 == 0;  // row strides and addresses are checked per block on the device
+  const long long work = (long long)rows * (vec ? cols / 8 : cols);
+  const int blocks = (int)std::max<long long>(1, std::min<long long>((work + 255) / 256, 1024));
   const float wd_factor = (float)(1.0 - (double)lr * (double)weight_decay);
   ProfScope prof(PK_EW_APPLY, st);
   const dim3 grid(blocks, nblocks);
   if (u_dtype == LSR_DTYPE_F32)
     blocks_apply_kernel<float><<<grid, 256, 0, st>>>(ptrs, lds, rows, cols, static_cast<const float*>(U), u_index,
-                                                     wd_factor, weight_decay != 0.f, -lr);
+                                                     wd_factor, weight_decay != 0.f, -lr, vec);
   else if (u_dtype == LSR_DTYPE_BF16)
     blocks_apply_kernel<bf16><<<grid, 256, 0, st>>>(ptrs, lds, rows, cols, static_cast<const bf16*>(U), u_index,
-                                                    wd_factor, weight_decay != 0.f, -lr);
+                                                    wd_factor, weight_decay != 0.f, -lr, vec);
   else
     blocks_apply_kernel<__half><<<grid, 256, 0, st>>>(ptrs, lds, rows, cols, static_cast<const __half*>(U), u_index,
-                                                      wd_factor, weight_decay != 0.f, -lr);
+                                                      wd_factor, weight_decay != 0.f, -lr, vec);
   return cudaGetLastError() == cudaSuccess ? LSR_OK : LSR_ERR_LAUNCH;
 }
 

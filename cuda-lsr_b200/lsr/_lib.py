@@ -79,6 +79,11 @@ SIGNATURES: dict[str, tuple] = {
     "lsr_kron_apply_f32": (
         c_int,
         [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "lsr_kron_dense_operator_f32": (
+        c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "lsr_kron_dense_apply_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "lsr_kron_dense_apply_f32": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "lsr_kron_reconstruct_f32": (
         c_int, [ctypes.POINTER(c_void_p), ctypes.POINTER(c_int), ctypes.POINTER(c_int), c_int, c_int, c_void_p,
                 c_void_p]),

@@ -62,11 +62,45 @@ def kron_sum(A: torch.Tensor, X: torch.Tensor, B: torch.Tensor, out: torch.Tenso
     return Y.view(X.shape) if out is None else out
 
 
+# Dense operators of small fp32 factors, W = sum_s A_s (x) B_s as a tf32 pair, kept per factor
+# tensors (identity, version counter, shape): applying the same factors again skips forming W.
+_DENSE_CACHE: dict = {}
+_DENSE_MAX_MN = 1024
+
+
+def _dense_operator(A3, B3, a_trans: bool):
+    m, n, S = A3.shape[1], B3.shape[1], A3.shape[0]
+    key = (A3.data_ptr(), A3._version, B3.data_ptr(), B3._version, a_trans, m, n, S, A3.device.index)
+    hit = _DENSE_CACHE.get(key)
+    if hit is not None:
+        return hit
+    if len(_DENSE_CACHE) >= 8:
+        _DENSE_CACHE.clear()
+    mn = m * n
+    Wh = torch.empty(mn, mn, dtype=torch.float32, device=A3.device)
+    Wl = torch.empty_like(Wh)
+    lib = _lib.load()
+    _lib.check(lib.lsr_kron_dense_operator_f32(A3.data_ptr(), int(a_trans), B3.data_ptr(), m, n, S, Wh.data_ptr(),
+                                               Wl.data_ptr(), _lib.stream_handle(A3.device)),
+               "lsr_kron_dense_operator_f32")
+    _DENSE_CACHE[key] = (Wh, Wl, A3, B3)  # the factors are held so their addresses stay theirs
+    return _DENSE_CACHE[key]
+
+
 def _kron_apply(X3, A3, B3, a_trans: bool, Y) -> None:
     batch, m, n = X3.shape
     S = A3.shape[0]
     f32 = X3.dtype == torch.float32
     lib = _lib.load()
+    if f32 and m * n <= _DENSE_MAX_MN and (m * n) % 4 == 0:
+        with torch.cuda.device(X3.device):
+            Wh, Wl, _, _ = _dense_operator(A3, B3, a_trans)
+            nb = lib.lsr_kron_dense_apply_workspace_bytes(batch, m * n)
+            ws = _lib.WORKSPACE.get(nb, X3.device)
+            _lib.check(lib.lsr_kron_dense_apply_f32(Wh.data_ptr(), Wl.data_ptr(), X3.data_ptr(), Y.data_ptr(), batch,
+                                                    m * n, ws.data_ptr(), nb, _lib.stream_handle(X3.device)),
+                       "lsr_kron_dense_apply_f32")
+        return
     with torch.cuda.device(X3.device):
         nb = lib.lsr_kron_apply_workspace_bytes(batch, m, n, S, int(f32))
         ws = _lib.WORKSPACE.get(nb, X3.device)

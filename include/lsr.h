@@ -261,6 +261,18 @@ LSR_API int lsr_kron_sum_f32(const float* A, const float* X, const float* B, flo
  * accuracy.  _bf16: bf16 operands.  _f32: fp32 operands (3xTF32).
  * ---------------------------------------------------------------------- */
 LSR_API size_t lsr_kron_apply_workspace_bytes(int batch, int m, int n, int nterms, int f32);
+/* Small-factor Kronecker apply split in two, for callers that apply the same
+ * factors to many right-hand-side batches (m n <= 1024, m n % 4 == 0):
+ *   lsr_kron_dense_operator_f32: W = sum_s A_s (x) B_s as a tf32 pair, Wh and Wl
+ *     fp32 [m n][m n] (A_s given transposed when a_trans, like kron_sum_out's
+ *     prepacked at = A^T, hft_fused.py:247-252);
+ *   lsr_kron_dense_apply_f32: Y [batch][m n] = X [batch][m n] W^T, one 3xTF32 GEMM.
+ * lsr_kron_apply_f32 does both per call. */
+LSR_API int lsr_kron_dense_operator_f32(const float* A, int a_trans, const float* B, int m, int n, int nterms,
+                                        float* Wh, float* Wl, lsr_stream_t stream);
+LSR_API size_t lsr_kron_dense_apply_workspace_bytes(int batch, int mn);
+LSR_API int lsr_kron_dense_apply_f32(const float* Wh, const float* Wl, const float* X, float* Y, int batch, int mn,
+                                     void* ws, size_t ws_bytes, lsr_stream_t stream);
 LSR_API int lsr_kron_apply_bf16(const void* A, int a_trans, const void* X, const void* B, float* Y, int batch,
                                 int m, int n, int nterms, void* ws, size_t ws_bytes, lsr_stream_t stream);
 LSR_API int lsr_kron_apply_f32(const float* A, int a_trans, const float* X, const float* B, float* Y, int batch,

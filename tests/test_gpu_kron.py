@@ -148,3 +148,20 @@ def test_native_reconstruct_general_shapes():
     ref = ok.reconstruct([f.cpu().numpy() for f in fs])
     assert W.shape == ref.shape == (24, 120)
     assert rel_fro(W.cpu().numpy(), ref) < TOL_F32
+
+
+def test_kron_sum_out_dense_operator_follows_factor_updates():
+    """Small factors run through a cached dense operator W = sum_s A_s (x) B_s: an in-place change of
+    the factors (a new version of the tensor) must be seen by the next call."""
+    import lsr.kron as K
+    g = torch.Generator(device="cuda").manual_seed(77)
+    x = torch.randn(300, 64, 8, device="cuda", generator=g)
+    at = torch.randn(4, 64, 64, device="cuda", generator=g) / 8
+    b = torch.randn(4, 8, 8, device="cuda", generator=g) / 3
+    out = torch.empty_like(x)
+    for _ in range(2):
+        K.kron_sum_out(x, at, b, out)
+        ref = torch.einsum("ski,mkl,sjl->mij", at.double(), x.double(), b.double())
+        assert rel_fro(out.cpu().numpy(), ref.cpu().numpy()) < TOL_F32
+        at.mul_(-0.5)
+        b.add_(0.1)

@@ -105,6 +105,26 @@ def test_ragged_shapes_vs_oracle(shape):
     assert rel_fro(out, ref) < TOL
 
 
+@pytest.mark.parametrize("shape", [(160, 480), (480, 160), (320, 320), (1600, 1600), (3, 320, 960), (3, 960, 320)])
+def test_narrow_tile_shapes(shape):
+    """Row counts that are multiples of 160 but not of 256 (GPT-2-XL's 1600) run on 160-wide tiles
+    and the transposed update (X'^T = X^T B); wide, tall and batched inputs against the reference
+    op sequence on this GPU and, for the small cases, the oracle."""
+    import lsr
+    g = torch.Generator().manual_seed(sum(shape))
+    G = (torch.randn(*shape, generator=g) * 0.02).bfloat16()
+    if len(shape) == 2:
+        out = lsr.zeropower_serial(G.cuda(), 5, 1e-7)
+    else:
+        out = lsr.zeropower_via_newtonschulz5(G.cuda(), 5, 1e-7)
+    assert out.shape == G.shape
+    ref = ns_torch(G.cuda(), 5, 1e-7)
+    assert rel_fro(_np(out), _np(ref)) < TOL
+    if len(shape) == 2 and max(shape) <= 480:
+        assert rel_fro(_np(out), om.zeropower(G.float().numpy(), 5, 1e-7)) < TOL
+    assert lsr._lib.device_status() == 0
+
+
 def test_zero_matrix_is_finite():
     import lsr
     out = lsr.zeropower_serial(torch.zeros(64, 128, device="cuda", dtype=torch.bfloat16), 5, 1e-7)

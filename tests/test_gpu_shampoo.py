@@ -95,7 +95,8 @@ def test_soap_config3_two_steps():
         print(f"config-3 SOAP step {t}: " + ", ".join(f"{k} {e:.2e}" for k, e in errs.items()) +
               f", sign differences {nflip}")
         assert errs["m"] < TOL and errs["v"] < TOL, (t, errs)
-        assert errs["L"] < 1e-5 and errs["R"] < 1e-5, (t, errs)
+        # statistics: bf16 operands, fp32 accumulation over K = 6400 (L) / 1600 (R) products
+        assert errs["L"] < 5e-5 and errs["R"] < 5e-5, (t, errs)
         assert errs["U_same_signs" if (t == 1 and nflip) else "U"] < TOL, (t, errs)
         if t == 2:
             assert errs["U"] < TOL, errs
