@@ -25,6 +25,7 @@ Rank 0 prints one JSON line.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -421,6 +422,10 @@ def run_e2e(args, params, grads, step, world, opt):
     a device snapshot, so step i's download (second copy stream) overlaps step
     i+1's compute. Every step still moves all of its bytes each way; the timed
     region ends when the last download has landed.
+
+    Under ZeRO-1 (world > 1) a rank uploads the gradients of the matrices it
+    owns and downloads the updated parameters it owns, so the ranks together
+    move every gradient and every parameter across PCIe exactly once per step.
     """
     if world == 1:
         need = list(range(len(params)))
@@ -430,11 +435,12 @@ def run_e2e(args, params, grads, step, world, opt):
     host_g = {i: torch.empty(grads[i].shape, dtype=torch.bfloat16, pin_memory=True) for i in need}
     for i in need:
         host_g[i].copy_(grads[i])
-    host_p = [torch.empty(p.shape, dtype=torch.bfloat16, pin_memory=True) for p in params]
+    host_p = [torch.empty(params[i].shape, dtype=torch.bfloat16, pin_memory=True) for i in need]
     h2d = sum(host_g[i].numel() * 2 for i in need)
     d2h = sum(h.numel() * 2 for h in host_p)
     gbuf = [{i: torch.empty_like(grads[i]) for i in need} for _ in range(2)]
-    snap = [torch.empty_like(p.data) for p in params]
+    snap = [torch.empty_like(params[i].data) for i in need]
+    mine = [params[i] for i in need]
     compute = torch.cuda.current_stream()
     up, down = torch.cuda.Stream(), torch.cuda.Stream()
     ev_up = [torch.cuda.Event() for _ in range(2)]
@@ -465,7 +471,7 @@ def run_e2e(args, params, grads, step, world, opt):
         step()
         ev_free[b].record(compute)
         compute.wait_event(ev_down)  # the previous download has read the snapshot
-        for p, s_ in zip(params, snap):
+        for p, s_ in zip(mine, snap):
             s_.copy_(p.data, non_blocking=True)
         ev_snap.record(compute)
         down.wait_event(ev_snap)
@@ -490,12 +496,15 @@ def run_e2e(args, params, grads, step, world, opt):
     barrier(world)
     ms = max_over_ranks(a.elapsed_time(b) / n, world)
     # the host copy is the step's result: check it against the device parameters
-    matches = all(torch.equal(h, p.data.cpu()) for h, p in zip(host_p, params))
+    matches = all(torch.equal(h, p.data.cpu()) for h, p in zip(host_p, mine))
     return {"value": round(ms, 3) if matches else None, "unit": "ms", "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h), "host_copy_matches_device": bool(matches), "valid": bool(matches),
             "steps": n, "path": "lsr.MuonAdamW.muon_step" if world == 1 else "lsr.dist.ShardedMuon.step",
             "pipelining": "double-buffered device gradients (upload of step i+1 during step i) and a device "
-                          "snapshot of the parameters (download of step i during step i+1); two copy streams"}
+                          "snapshot of the parameters (download of step i during step i+1); two copy streams",
+            "copies": "all gradients in, all parameters out" if world == 1 else
+                      "per rank: the gradients in and the updated parameters out of the matrices it owns "
+                      "(every matrix crosses PCIe once per step across the ranks)"}
 
 
 def load_traffic(kind: str):
@@ -514,24 +523,55 @@ def load_traffic(kind: str):
 # Per-row workloads (not the headline line): --workload cfg1|cfg2|cfg3|cfg5
 # ---------------------------------------------------------------------------
 
-def _time_gpu(fn, warmup, iters, flush_bytes=256 << 20):
+def _nvtx(name):
+    """An NVTX push/pop range around a timed phase, so an ncu capture can select that phase's
+    kernels (`ncu --nvtx --nvtx-include "<name>/" ...`)."""
+    return torch.cuda.nvtx.range(name) if name else contextlib.nullcontext()
+
+
+def _time_gpu(fn, warmup, iters, flush_bytes=256 << 20, name=None):
     """Mean ms of fn() over `iters` runs, L2 flushed (a buffer larger than L2 is written) before each
-    unless flush_bytes is 0."""
+    unless flush_bytes is 0. Warm-up and timed runs sit inside the NVTX range `name`."""
     flush = torch.empty(flush_bytes, dtype=torch.uint8, device="cuda") if flush_bytes else None
-    for _ in range(warmup):
-        fn()
-    torch.cuda.synchronize()
-    tot = 0.0
-    for _ in range(iters):
-        if flush is not None:
-            flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        fn()
-        b.record()
-        b.synchronize()
-        tot += a.elapsed_time(b)
+    with _nvtx(name):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(iters):
+            if flush is not None:
+                flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            tot += a.elapsed_time(b)
     return tot / iters
+
+
+def _median_loop_ms(fn, warmup=20, iters=100, repeats=7, name=None):
+    """Per-call ms as the reference's microbenchmarks time their kernels (median_ms,
+    hft_fused.py:403-432; median_us, kron_cuda.py:91-114): `iters` back-to-back calls between two
+    events, median over `repeats`. Host launch cost overlaps the GPU here, so the figure is the
+    larger of the two per call. Also returns the host microseconds per call (no synchronisation
+    inside the loop)."""
+    with _nvtx(name):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        vals, host = [], []
+        for _ in range(repeats):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            t0 = time.perf_counter()
+            for _ in range(iters):
+                fn()
+            host.append((time.perf_counter() - t0) * 1e6 / iters)
+            b.record()
+            b.synchronize()
+            vals.append(a.elapsed_time(b) / iters)
+    return statistics.median(vals), statistics.median(host)
 
 
 def _time_cpu(fn, reps=2):
@@ -569,10 +609,68 @@ def _torch_batched_coupled_newton(A, root, tolerance=1e-6, max_iterations=100):
     return X
 
 
+def run_cfg5_sharded(args, world: int) -> None:
+    """The GPT-2-XL SOAP step under ZeRO-1 on `world` GPUs (one process each, NCCL): every rank builds
+    the same 192 matrices (seed 5), owns 1/world of the 2016 blocks (greedy by flops), and the
+    directions are all-gathered in the reference's default communication dtype (float16). Time per
+    step: CUDA events on each rank, max over ranks; total work is fixed (strong scaling)."""
+    import torch.distributed as dist
+    from lsr import shampoo as SH
+    rank, local_rank = int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    g = torch.Generator().manual_seed(5)
+    shapes = [s for _ in range(args.layers) for s in LAYER_SHAPES]
+    params = [torch.nn.Parameter((torch.randn(*s, generator=g) * 0.02).bfloat16().to(dev)) for s in shapes]
+    for p in params:
+        p.grad = (torch.randn(*p.shape, generator=g) * 0.01).bfloat16().to(dev)
+    opt = SH.DistributedShampoo(params, lr=0.02, betas=(0.95, 0.95), epsilon=1e-8, weight_decay=0.01,
+                                max_preconditioner_dim=1024, precondition_frequency=10 ** 9,
+                                start_preconditioning_step=10 ** 9, preconditioner_config=SH.DefaultSOAPConfig,
+                                distributed_config=SH.DDPDistributedConfig())
+    opt.step()  # builds the block groups
+    gq = torch.Generator(device=dev).manual_seed(5 + rank)
+    for _, grp, _ in opt._groups:
+        if grp is None:
+            continue
+        n, r, c = grp.stack.shape
+        grp.QL = torch.linalg.qr(torch.randn(n, r, r, generator=gq, device=dev))[0].bfloat16().contiguous()
+        grp.QR = torch.linalg.qr(torch.randn(n, c, c, generator=gq, device=dev))[0].bfloat16().contiguous()
+    for _ in range(args.warmup):
+        opt.step()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        opt.step()
+    b.record()
+    barrier(world)
+    ms = max_over_ranks(a.elapsed_time(b) / args.steps, world)
+    if rank == 0:
+        from oracle import shampoo as osh
+        fl = sum(osh.soap_flops(r, c) * len(lst) for (r, c), _, lst in opt._groups)
+        peaks = measured_peaks()
+        print(json.dumps({"workload": f"cfg5: GPT-2-XL SOAP step, {args.layers} layers, 2016 blocks at 1024, "
+                                      f"ZeRO-1 over {world} GPUs, float16 exchange",
+                          "value": ms, "unit": "ms", "n_gpus": world, "algorithmic_tflop": fl / 1e12,
+                          "tflops": fl / ms / 1e9,
+                          "per_gpu_frac_of_sustained": fl / ms / 1e9 / world / peaks["bf16_tflops_sustained"],
+                          "steps": args.steps, "warmup": args.warmup, "scaling": "strong"}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def run_workload(args) -> None:
     import lsr
     import lsr.kron as K
     from lsr import shampoo as SH
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        if args.workload != "cfg5":
+            raise SystemExit(f"--workload {args.workload} runs on one GPU; cfg5 also runs sharded under torchrun")
+        run_cfg5_sharded(args, world)
+        return
     torch.cuda.set_device(0)
     peaks = measured_peaks()
     dev = torch.device("cuda", 0)
@@ -583,7 +681,8 @@ def run_workload(args) -> None:
         wide = (torch.randn(12, 768, 3072, generator=g) * 0.02).bfloat16().to(dev)
         tall = (torch.randn(12, 3072, 768, generator=g) * 0.02).bfloat16().to(dev)
         ms = _time_gpu(lambda: (lsr.zeropower_via_newtonschulz5(wide, 5, 1e-7),
-                                lsr.zeropower_via_newtonschulz5(tall, 5, 1e-7)), args.warmup, args.steps)
+                                lsr.zeropower_via_newtonschulz5(tall, 5, 1e-7)), args.warmup, args.steps,
+                      name="cfg1")
         fl = 24 * ns_dense_flops((768, 3072))
         from oracle import muon as om
         G1 = wide[0].float().cpu().numpy()
@@ -602,7 +701,8 @@ def run_workload(args) -> None:
                                     ("bf16", A.bfloat16(), X.bfloat16(), B.bfloat16(),
                                      peaks["bf16_tflops_sustained"])):
             Y = torch.empty(64, 1024, 1024, device=dev)
-            ms = _time_gpu(lambda: K.kron_sum(a, x, b, out=Y), args.warmup, args.steps)
+            ms = _time_gpu(lambda: K.kron_sum(a, x, b, out=Y), args.warmup, args.steps,
+                           name="cfg2." + name.split()[0])
             nbytes = x.numel() * x.element_size() + Y.numel() * 4
             line = {"workload": f"cfg2: Kronecker sum (A+B)vec(X), A,B 1024^2, 64 RHS, {name}", "value": ms,
                     "unit": "ms", "algorithmic_gflop": fl / 1e9, "tflops": fl / ms / 1e9,
@@ -631,13 +731,14 @@ def run_workload(args) -> None:
             L = torch.zeros(1, r, r, device=dev)
             R = torch.zeros(1, c, c, device=dev)
             ms_stats = _time_gpu(lambda: (SH.gram_update(G, L, 0, 0.0, 1.0), SH.gram_update(G, R, 1, 0.0, 1.0)),
-                                 args.warmup, args.steps)
+                                 args.warmup, args.steps, name="cfg3.stats")
             Lr, Rr = orth(r, 1), orth(c, 1)  # stand-ins with the shapes of the precomputed inverse roots
-            ms_apply = _time_gpu(lambda: SH.shampoo_direction(G, Lr, Rr), args.warmup, args.steps)
+            ms_apply = _time_gpu(lambda: SH.shampoo_direction(G, Lr, Rr), args.warmup, args.steps,
+                                 name="cfg3.shampoo")
             m = torch.zeros(1, r, c, device=dev)
             v = torch.zeros(1, r, c, device=dev)
             ms_soap = _time_gpu(lambda: SH.soap_direction(G, None, None, Lr, Rr, m, v, 0.95, 0.95, 1e-8, 1, False),
-                                args.warmup, args.steps)
+                                args.warmup, args.steps, name="cfg3.soap")
             f_stats = 2.0 * r * r * c + 2.0 * r * c * c
             for name, ms, fl in (("statistics L=GG^T, R=G^TG", ms_stats, f_stats),
                                  ("Shampoo apply L^-1/4 G R^-1/4", ms_apply, f_stats),
@@ -658,7 +759,7 @@ def run_workload(args) -> None:
             for _, grp, _ in opt._groups:
                 n, r, c = grp.stack.shape
                 grp.QL, grp.QR = orth(r, n), orth(c, n)
-            ms = _time_gpu(opt.step, args.warmup, args.steps)
+            ms = _time_gpu(opt.step, args.warmup, args.steps, name="cfg5.step")
             from lsr import _lib
             _lib.profile_enable(True)
             _lib.profile_read(reset=True)
@@ -673,12 +774,67 @@ def run_workload(args) -> None:
                           "value": ms, "unit": "ms", "algorithmic_tflop": fl / 1e12, "tflops": fl / ms / 1e9,
                           "frac_of_sustained": fl / ms / 1e9 / peaks["bf16_tflops_sustained"],
                           "per_kind_ms_one_step": kinds})
+    elif w in ("refresh", "cfg5s"):
+        # refresh: the periodic SOAP eigenbasis refresh of the config-5 blocks (every L and R factor,
+        # statistics of a few seeded steps): power iteration with Householder QR from the current
+        # bases (lsr_eigenbasis_refresh_f32, one iteration, as every refresh after the first), timed
+        # beside an fp32 torch.linalg.eigh of a sample of the same factors (extrapolated by count).
+        # cfg5s: the Shampoo step (Adam grafting, inverse 4th roots fixed) on the config-5 blocks.
+        g = torch.Generator().manual_seed(5)
+        shapes = [s for _ in range(args.layers) for s in LAYER_SHAPES]
+        params = [torch.nn.Parameter((torch.randn(*s, generator=g) * 0.02).bfloat16().to(dev)) for s in shapes]
+        for p in params:
+            p.grad = (torch.randn(*p.shape, generator=g) * 0.01).bfloat16().to(dev)
+        soap = w == "refresh"
+        opt = SH.DistributedShampoo(params, lr=0.02, betas=(0.95, 0.95), epsilon=1e-8, weight_decay=0.01,
+                                    max_preconditioner_dim=1024, precondition_frequency=10 ** 9,
+                                    start_preconditioning_step=1 if not soap else 10 ** 9,
+                                    preconditioner_config=SH.DefaultSOAPConfig if soap else None,
+                                    grafting_config=None if soap else SH.AdamPreconditionerConfig(0.95, 1e-8))
+        for _ in range(3):
+            opt.step()  # statistics of three steps
+        if soap:
+            for _, grp, _ in opt._groups:
+                opt._refresh(grp, 1e-8)  # first refresh (from the identity basis, first_iterations)
+            torch.cuda.synchronize()
+            ms = _time_gpu(lambda: [opt._refresh(grp, 1e-8) for _, grp, _ in opt._groups], args.warmup, args.steps,
+                           name="refresh")
+            nfac = sum(2 * len(grp.refs) for _, grp, _ in opt._groups)
+            # eigh of a sample: the first 4 blocks of every shape, both factors, scaled by count
+            t_eigh, n_eigh = 0.0, 0
+            for (r, c), grp, _ in opt._groups:
+                k = min(4, len(grp.refs))
+                Ls, Rs = grp.L[:k].clone(), grp.R[:k].clone()
+                ms_s = _time_gpu(lambda: (torch.linalg.eigh(Ls), torch.linalg.eigh(Rs)), 1, 1, flush_bytes=0)
+                t_eigh += ms_s * len(grp.refs) / k
+                n_eigh += 2 * k
+            lines.append({"workload": f"refresh: SOAP eigenbasis refresh of the config-5 blocks ({args.layers} layers, "
+                                      f"{nfac} factors of <= 1024^2), one power iteration + Householder QR",
+                          "value": ms, "unit": "ms", "torch_eigh_fp32_ms_extrapolated": t_eigh,
+                          "eigh_sample_factors": n_eigh, "speedup_vs_eigh": t_eigh / ms})
+        else:
+            gq = torch.Generator(device=dev).manual_seed(5)
+            for (r, c), grp, _ in opt._groups:  # stand-ins with the shapes of the inverse roots
+                n = len(grp.refs)
+                grp.QL = torch.linalg.qr(torch.randn(n, r, r, generator=gq, device=dev))[0].bfloat16().contiguous()
+                grp.QR = torch.linalg.qr(torch.randn(n, c, c, generator=gq, device=dev))[0].bfloat16().contiguous()
+                grp.have_roots = True
+            ms = _time_gpu(opt.step, args.warmup, args.steps, name="cfg5s.step")
+            from oracle import shampoo as osh
+            # statistics and the two-sided apply: 2 (2 r^2 c + 2 r c^2) = 2/3 of the SOAP count
+            fl = sum(osh.soap_flops(r, c) * len(grp.refs) * 2 / 3 for (r, c), grp, _ in opt._groups)
+            lines.append({"workload": f"cfg5s: GPT-2-XL Shampoo step with Adam grafting, {args.layers} layers, "
+                                      f"{sum(len(grp.refs) for _, grp, _ in opt._groups)} blocks at 1024, 1 GPU",
+                          "value": ms, "unit": "ms",
+                          "algorithmic_tflop": fl / 1e12, "tflops": fl / ms / 1e9,
+                          "frac_of_sustained": fl / ms / 1e9 / peaks["bf16_tflops_sustained"]})
     elif w == "kron64x8":
         # The reference's own Kronecker-sum sweep (hft_fused.py:856-862): x [M, 64, 8], S terms
         # A_s [64,64] / sqrt(64), B_s [8,8] / sqrt(8), at = A^T prepacked, fp32 (TF32 off). Its
         # kron_sum_64x8_kernel (built from the staged hft_fused.py by its own load_inline) and
-        # lsr.kron.kron_sum_out run on the same inputs and GPU, timed the same way (no L2 flush, as
-        # the reference's median_ms); results are compared against the fp64 product.
+        # lsr.kron.kron_sum_out run on the same inputs and GPU, both timed with the reference's own
+        # method (median_ms: 100 back-to-back calls between two events, median of 7, no L2 flush);
+        # results are compared against the fp64 product.
         ref = load_reference_module("hft_fused")
         torch.backends.cuda.matmul.allow_tf32 = False
         for M in (256, 1024, 4096, 16384):
@@ -693,20 +849,72 @@ def run_workload(args) -> None:
 
                 def ours():
                     K.kron_sum_out(X, AT, B, Y)
-                ms = _time_gpu(ours, args.warmup, max(args.steps, 20), flush_bytes=0)
+                ms, host_us = _median_loop_ms(ours, name=f"kron64x8.M{M}.S{S}")
                 err = ((Y.double() - Yd).norm() / Yd.norm()).item()
                 line = {"workload": f"kron64x8: x [{M},64,8], S={S}, fp32", "value": ms, "unit": "ms",
-                        "rel_err_vs_fp64": err}
+                        "host_us_per_call": host_us, "rel_err_vs_fp64": err,
+                        "timing": "median of 7 x (100 back-to-back calls between two events)"}
                 if ref is not None:
                     Yr = torch.empty_like(X)
 
                     def theirs():
                         ref.ext.kron_sum_out(X, AT, B, Yr)
-                    ms_ref = _time_gpu(theirs, args.warmup, max(args.steps, 20), flush_bytes=0)
-                    line.update({"reference_kernel_ms": ms_ref, "speedup_vs_reference_kernel": ms_ref / ms,
+                    ms_ref, host_ref = _median_loop_ms(theirs)
+                    line.update({"reference_kernel_ms": ms_ref, "reference_host_us_per_call": host_ref,
+                                 "speedup_vs_reference_kernel": ms_ref / ms,
                                  "reference_rel_err_vs_fp64": ((Yr.double() - Yd).norm() / Yd.norm()).item()})
                 else:
                     line["reference_kernel_ms"] = None
+                lines.append(line)
+    elif w == "kronrec":
+        # The reference's tiny-factor reconstruction sweep (kron_cuda.py:705-1040): W [16, 768] =
+        # sum_s F_0[s] x ... x F_{K-1}[s] for the three equivalent factorisations K = 3, 4, 5 of
+        # make_equivalent_factors (kron_cuda.py:169-225), S in its default list. Its Triton
+        # native_reconstruct (best block of 64..512, as its find_best_native picks) and
+        # lsr.kron.native_reconstruct run on the same factors and GPU, both timed with the
+        # reference's median_us method (200 back-to-back calls between two events, median of 7).
+        ref = load_reference_module("kron_cuda")
+        for S in (1, 2, 4, 8, 16, 32, 64, 96, 128, 192, 256):
+            if ref is not None:
+                reps = ref.make_equivalent_factors(S, seed=17)
+            else:  # the same construction: K=5 factors, merged pairwise into the K=4 and K=3 lists
+                gk = torch.Generator().manual_seed(17 + S)
+                f = [(0.5 * torch.randn(S, *sh, generator=gk)).to(dev)
+                     for sh in ((1, 3), (2, 4), (2, 4), (2, 4), (2, 4))]
+
+                def bk(a, b):
+                    return torch.einsum("sij,skl->sikjl", a, b).reshape(a.shape[0], a.shape[1] * b.shape[1],
+                                                                        a.shape[2] * b.shape[2])
+                g01 = bk(f[0], f[1])
+                reps = {5: f, 4: [g01] + f[2:], 3: [bk(g01, f[2])] + f[3:]}
+            W64 = None
+            for Kf in (5, 4, 3):
+                fac = reps[Kf]
+                out = torch.empty(16, 768, device=dev)
+                ms, host_us = _median_loop_ms(lambda: K.native_reconstruct(fac, Kf, out), warmup=10, iters=200,
+                                              name=f"kronrec.K{Kf}.S{S}")
+                if W64 is None:  # fp64 reference value of W from the K=5 factors
+                    t = reps[5][0].double().cpu()
+                    for fk in reps[5][1:]:
+                        fk = fk.double().cpu()
+                        t = torch.einsum("sij,skl->sikjl", t, fk).reshape(S, t.shape[1] * fk.shape[1],
+                                                                          t.shape[2] * fk.shape[2])
+                    W64 = t.sum(0)
+                err = ((out.double().cpu() - W64).norm() / W64.norm()).item()
+                line = {"workload": f"kronrec: W 16x768, K={Kf}, S={S}, fp32", "value": ms, "unit": "ms",
+                        "host_us_per_call": host_us, "rel_err_vs_fp64": err,
+                        "timing": "median of 7 x (200 back-to-back calls between two events)"}
+                if ref is not None:
+                    outr = torch.empty(16, 768, device=dev)
+                    best, _ = ref.find_best_native(fac, Kf, outr)
+                    ref.native_reconstruct(fac, Kf, outr, block=best["block"])
+                    torch.cuda.synchronize()
+                    line.update({"reference_triton_ms": best["us"] / 1e3, "reference_block": best["block"],
+                                 "speedup_vs_reference_triton": best["us"] / 1e3 / ms,
+                                 "reference_rel_err_vs_fp64": ((outr.double().cpu() - W64).norm()
+                                                               / W64.norm()).item()})
+                else:
+                    line["reference_triton_ms"] = None
                 lines.append(line)
     elif w == "f1":
         # Batched coupled Newton inverse roots on the reference's full bucket list
@@ -728,7 +936,8 @@ def run_workload(args) -> None:
             ridge[-max(1, int(round(B * 0.15))):] = 1e-5
             A = (A + ridge[:, None, None] * torch.eye(n)).contiguous().to(dev)
             _, iters, _ = lsr.batched_coupled_newton(A, root)
-            ms = _time_gpu(lambda: lsr.batched_coupled_newton(A, root), args.warmup, args.steps)
+            ms = _time_gpu(lambda: lsr.batched_coupled_newton(A, root), args.warmup, args.steps,
+                           name=f"f1.n{n}.root{root}")
             ms_ref = _time_gpu(lambda: _torch_batched_coupled_newton(A, root), 1, max(1, args.steps // 2))
             from lsr import newton as NW
             ms_tc = _time_gpu(lambda: NW._run(A, root, 0.0, 1e-6, 100, use_tf32=True), args.warmup, args.steps)
@@ -799,7 +1008,9 @@ def main(argv=None) -> int:
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="nccl",
                     help="N>1: parameter exchange (peer-memory push or NCCL all-gather)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["muon", "cfg1", "cfg2", "cfg3", "cfg5", "f1", "muon_torch", "kron64x8"],
+    ap.add_argument("--workload", choices=["muon", "cfg1", "cfg2", "cfg3", "cfg5", "cfg5s", "refresh", "f1", "muon_torch",
+                                           "kronrec",
+                                           "kron64x8"],
                     default="muon",
                     help="muon = the headline GPT-2-XL Muon step (default); cfgN = per-row workloads")
     args = ap.parse_args(argv)

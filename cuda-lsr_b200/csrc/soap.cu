@@ -37,15 +37,55 @@ Operand bmat(const void* base, int rows, int cols, int batch, int mn) {
   return Operand{base, rows, cols, cols, (long long)rows * cols, batch, mn};
 }
 
-int set_pairs(GemmParams& p, const Operand (*pairs)[2], int nseg, int kblocks) {
+// Launch shape of a block-stack GEMM whose output is r x c: CTA pairs (256-row
+// tiles, half of operand B per CTA) when r spans more than one 128-row tile,
+// and two K blocks per pipeline stage (one 4-D TMA box per operand) when every
+// dimension is a whole number of 64-element blocks -- the shape that runs the
+// Newton-Schulz update fastest.
+struct Shape {
+  bool pair;
+  int ks;
+};
+
+Shape soap_shape(int r, int c) { return Shape{r > BM, (r % BK == 0 && c % BK == 0) ? 2 : 1}; }
+
+
+
+int set_pairs(GemmParams& p, const Operand (*pairs)[2], int nseg, int kblocks, Shape sh) {
   int rc = 0;
+  const int bbox = sh.pair ? S_BN / 2 : S_BN;
   for (int t = 0; t < nseg && !rc; ++t) {
     p.g[0].seg[t] = SegDesc{kblocks, pairs[t][0].mn, pairs[t][1].mn, 0, 0, 0};
-    rc = make_operand_map(&p.mapA[0][t], pairs[t][0], false, S_BN, &p.g[0].seg[t].a_mn);
-    if (!rc) rc = make_operand_map(&p.mapB[0][t], pairs[t][1], true, S_BN, &p.g[0].seg[t].b_mn);
+    rc = make_operand_map(&p.mapA[0][t], pairs[t][0], false, S_BN, &p.g[0].seg[t].a_mn, sh.ks);
+    if (!rc) rc = make_operand_map(&p.mapB[0][t], pairs[t][1], true, bbox, &p.g[0].seg[t].b_mn, sh.ks);
   }
   p.g[0].nseg = nseg;
   return rc;
+}
+
+// Two-block stages only where at least two of them fit beside the epilogue's staging buffers.
+template <int EPI, int PAIR>
+constexpr bool ks2_fits() {
+  return GemmSmem<S_BN, 2, EPI, PAIR, 2>::TOTAL <= 232448;
+}
+
+// The shape launch_soap<EPI> uses: two-block stages only where they fit.
+template <int EPI>
+Shape effective(Shape sh) {
+  const bool fits = sh.pair ? ks2_fits<EPI, 1>() : ks2_fits<EPI, 0>();
+  return Shape{sh.pair, fits ? sh.ks : 1};
+}
+
+template <int EPI>
+int launch_soap(GemmParams& p, Shape sh, cudaStream_t st) {
+  if (sh.pair) {
+    if constexpr (ks2_fits<EPI, 1>())
+      if (sh.ks == 2) return launch_gemm<S_BN, EPI, default_stages<EPI, 1, S_BN, 2>(), 0, 0, 1, 2>(p, st);
+    return launch_gemm<S_BN, EPI, default_stages<EPI, 1, S_BN, 1>(), 0, 0, 1, 1>(p, st);
+  }
+  if constexpr (ks2_fits<EPI, 0>())
+    if (sh.ks == 2) return launch_gemm<S_BN, EPI, default_stages<EPI, 0, S_BN, 2>(), 0, 0, 0, 2>(p, st);
+  return launch_gemm<S_BN, EPI>(p, st);
 }
 
 void out_desc(GroupDesc& G, int batch, int r, int c, void* out, void* out2) {
@@ -296,6 +336,9 @@ int lsr_soap_direction_bf16(const void* G, float* L, float* R, const void* QL, c
   // fp32-level accuracy with bf16 tensor-core operands. Each two-sided product
   // runs the cheaper association first.
   const bool right_first = c > r;
+  const Shape sh_split = effective<EPI_SPLIT_BF16X2>(soap_shape(r, c));
+  const Shape sh_adam = effective<EPI_SOAP_ADAM>(soap_shape(r, c));
+  const Shape sh_f32 = effective<EPI_STORE_F32>(soap_shape(r, c));
   // ---- G' = Q_L^T G Q_R, Adam fused into the second GEMM's epilogue
   {
     GemmParams p{};
@@ -303,12 +346,12 @@ int lsr_soap_direction_bf16(const void* G, float* L, float* R, const void* QL, c
     out_desc(p.g[0], B, r, c, Ph, Pl);
     if (right_first) {  // S = G Q_R : (i,k) = G[i][k], (j,k) = Q_R[k][j]
       const Operand pr[1][2] = {{bmat(G, r, c, B, 0), bmat(QR, c, c, B, 1)}};
-      rc = set_pairs(p, pr, 1, cdiv(c, BK));
+      rc = set_pairs(p, pr, 1, cdiv(c, BK), sh_split);
     } else {  // T = Q_L^T G : (i,k) = Q_L[k][i], (j,k) = G[k][j]
       const Operand pr[1][2] = {{bmat(QL, r, r, B, 1), bmat(G, r, c, B, 1)}};
-      rc = set_pairs(p, pr, 1, cdiv(r, BK));
+      rc = set_pairs(p, pr, 1, cdiv(r, BK), sh_split);
     }
-    if (!rc) rc = launch_gemm<S_BN, EPI_SPLIT_BF16X2>(p, st);
+    if (!rc) rc = launch_soap<EPI_SPLIT_BF16X2>(p, sh_split, st);
     if (rc) return rc;
   }
   {
@@ -325,12 +368,12 @@ int lsr_soap_direction_bf16(const void* G, float* L, float* R, const void* QL, c
     Gd.eps = eps;
     if (right_first) {  // G' = Q_L^T S : (i,k) = Q_L[k][i], (j,k) = S[k][j]
       const Operand pr[2][2] = {{bmat(QL, r, r, B, 1), bmat(Ph, r, c, B, 1)}, {bmat(QL, r, r, B, 1), bmat(Pl, r, c, B, 1)}};
-      rc = set_pairs(p, pr, 2, cdiv(r, BK));
+      rc = set_pairs(p, pr, 2, cdiv(r, BK), sh_adam);
     } else {  // G' = T Q_R : (i,k) = T[i][k], (j,k) = Q_R[k][j]
       const Operand pr[2][2] = {{bmat(Ph, r, c, B, 0), bmat(QR, c, c, B, 1)}, {bmat(Pl, r, c, B, 0), bmat(QR, c, c, B, 1)}};
-      rc = set_pairs(p, pr, 2, cdiv(c, BK));
+      rc = set_pairs(p, pr, 2, cdiv(c, BK), sh_adam);
     }
-    if (!rc) rc = launch_gemm<S_BN, EPI_SOAP_ADAM>(p, st);
+    if (!rc) rc = launch_soap<EPI_SOAP_ADAM>(p, sh_adam, st);
     if (rc) return rc;
   }
   // ---- U = Q_L U' Q_R^T
@@ -340,12 +383,12 @@ int lsr_soap_direction_bf16(const void* G, float* L, float* R, const void* QL, c
     out_desc(p.g[0], B, r, c, Ph, Pl);
     if (right_first) {  // V = U' Q_R^T : (i,k) = U'[i][k], (j,k) = Q_R[j][k]
       const Operand pr[2][2] = {{bmat(Uh, r, c, B, 0), bmat(QR, c, c, B, 0)}, {bmat(Ul, r, c, B, 0), bmat(QR, c, c, B, 0)}};
-      rc = set_pairs(p, pr, 2, cdiv(c, BK));
+      rc = set_pairs(p, pr, 2, cdiv(c, BK), sh_split);
     } else {  // T = Q_L U' : (i,k) = Q_L[i][k], (j,k) = U'[k][j]
       const Operand pr[2][2] = {{bmat(QL, r, r, B, 0), bmat(Uh, r, c, B, 1)}, {bmat(QL, r, r, B, 0), bmat(Ul, r, c, B, 1)}};
-      rc = set_pairs(p, pr, 2, cdiv(r, BK));
+      rc = set_pairs(p, pr, 2, cdiv(r, BK), sh_split);
     }
-    if (!rc) rc = launch_gemm<S_BN, EPI_SPLIT_BF16X2>(p, st);
+    if (!rc) rc = launch_soap<EPI_SPLIT_BF16X2>(p, sh_split, st);
     if (rc) return rc;
   }
   GemmParams p{};
@@ -353,12 +396,12 @@ int lsr_soap_direction_bf16(const void* G, float* L, float* R, const void* QL, c
   out_desc(p.g[0], B, r, c, U, nullptr);
   if (right_first) {  // U = Q_L V : (i,k) = Q_L[i][k], (j,k) = V[k][j]
     const Operand pr[2][2] = {{bmat(QL, r, r, B, 0), bmat(Ph, r, c, B, 1)}, {bmat(QL, r, r, B, 0), bmat(Pl, r, c, B, 1)}};
-    rc = set_pairs(p, pr, 2, cdiv(r, BK));
+    rc = set_pairs(p, pr, 2, cdiv(r, BK), sh_f32);
   } else {  // U = T Q_R^T : (i,k) = T[i][k], (j,k) = Q_R[j][k]
     const Operand pr[2][2] = {{bmat(Ph, r, c, B, 0), bmat(QR, c, c, B, 0)}, {bmat(Pl, r, c, B, 0), bmat(QR, c, c, B, 0)}};
-    rc = set_pairs(p, pr, 2, cdiv(c, BK));
+    rc = set_pairs(p, pr, 2, cdiv(c, BK), sh_f32);
   }
-  return rc ? rc : launch_gemm<S_BN, EPI_STORE_F32>(p, st);
+  return rc ? rc : launch_soap<EPI_STORE_F32>(p, sh_f32, st);
 }
 
 size_t lsr_shampoo_workspace_bytes(int batch, int rows, int cols) {

@@ -4,8 +4,9 @@ The reference implements its Muon path in Python / torch (muon_lm_ddp.py:296-696
 adjusted_muon_lr, zeropower_serial, zeropower_batched_oriented, MuonAdamW),
 so there is nothing to compile, and its Kronecker-sum kernel
 (kron_sum_64x8_kernel, hft_fused.py:89-319) is CUDA source that hft_fused.py
-builds itself with torch's load_inline when imported on a GPU machine. This
-recipe copies those two modules, unmodified, from a cuda-lsr checkout into
+builds itself with torch's load_inline when imported on a GPU machine. The same holds
+for kron_cuda.py (tiny-factor reconstruction, Triton kernels compiled by Triton on the GPU). This
+recipe copies those three modules, unmodified, from a cuda-lsr checkout into
 ``oracle/_ref/`` (git-ignored; it travels with the working tree to the machine
 that runs the benchmark, where the checkout is absent) and records their
 SHA-256 beside them:
@@ -17,8 +18,9 @@ Muon module and time the reference's own ``MuonAdamW.muon_step`` on the host
 cores (``cpu_baseline.kind = "reference"``); without it they fall back to the
 numpy restatement in ``oracle/muon.py`` (``kind = "port"``). ``bench.py
 --workload kron64x8`` imports the staged hft_fused.py to time the reference's
-kernel beside liblsr's on the same GPU. Nothing in the product (the ``lsr``
-package) imports them.
+kernel beside liblsr's on the same GPU, and ``--workload kronrec`` imports the staged
+kron_cuda.py to time the reference's Triton tiny-factor reconstruction the same way. Nothing in the
+product (the ``lsr`` package) imports them.
 """
 from __future__ import annotations
 
@@ -30,7 +32,7 @@ from pathlib import Path
 
 REF_DIR = Path(__file__).resolve().parent / "_ref"
 MODULE = "muon_lm_ddp.py"
-MODULES = (MODULE, "hft_fused.py")
+MODULES = (MODULE, "hft_fused.py", "kron_cuda.py")
 
 
 def stage(reference: str | Path) -> Path | None:

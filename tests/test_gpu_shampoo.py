@@ -23,7 +23,7 @@ def _orth(n, g, batch):
     return Q.to(torch.bfloat16)
 
 
-@pytest.mark.parametrize("shape", [(2, 256, 1024), (2, 512, 256), (1, 1600, 640)])
+@pytest.mark.parametrize("shape", [(2, 256, 1024), (2, 512, 256), (1, 1600, 640), (2, 200, 136), (3, 96, 72)])
 def test_soap_direction(shape):
     from lsr.shampoo import soap_direction
     n, r, c = shape
