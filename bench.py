@@ -916,6 +916,100 @@ def run_workload(args) -> None:
                 else:
                     line["reference_triton_ms"] = None
                 lines.append(line)
+    elif w == "hawkes":
+        # The reference's Hawkes event-update benchmark (benchmark_hawkes, hft.py:615-800): 128 assets
+        # x 8 event types (D = 1024), N in {1024, 8192, 32768} streams, inputs drawn as it draws them.
+        # lsr.hawkes and the reference's Triton kernels (function definitions of the staged hft.py)
+        # on the same inputs and GPU, both timed with the reference's method (median of 7 x 100
+        # back-to-back calls). HBM-bound: 8 bytes per state entry (state in, out out); the 4 MB
+        # dense K stays in L2.
+        from lsr import hawkes as H
+        from oracle import stage_reference
+        try:
+            import triton
+            ref = stage_reference.load_functions(
+                "hft.py", ["hawkes_dense_kernel", "hawkes_kron_kernel", "hawkes_dense", "hawkes_kron"],
+                {"torch": torch, "triton": triton, "tl": triton.language})
+        except ImportError:
+            ref = None
+        NA, NE = 128, 8
+        g = torch.Generator(device=dev).manual_seed(123)
+        KA = (torch.rand(NA, NA, device=dev, generator=g) * 0.02).contiguous()
+        KE = (torch.rand(NE, NE, device=dev, generator=g) * 0.02).contiguous()
+        Kcol = torch.kron(KA, KE).T.contiguous()
+        D = NA * NE
+        for N in (1024, 8192, 32768):
+            state = torch.randn(N, D, device=dev, generator=g)
+            ea = torch.randint(0, NA, (N,), device=dev, generator=g, dtype=torch.int32)
+            et = torch.randint(0, NE, (N,), device=dev, generator=g, dtype=torch.int32)
+            ev = (ea * NE + et).contiguous()
+            decay = (0.90 + 0.099 * torch.rand(N, device=dev, generator=g)).contiguous()
+            nbytes = 8.0 * N * D
+            for kind in ("dense", "kron"):
+                out = torch.empty_like(state)
+                if kind == "dense":
+                    ours = lambda: H.hawkes_dense(state, ev, decay, Kcol, out)  # noqa: E731
+                    theirs = (lambda o: ref["hawkes_dense"](state, ev, decay, Kcol, o)) if ref else None
+                else:
+                    ours = lambda: H.hawkes_kron(state, ea, et, decay, KA, KE, out)  # noqa: E731
+                    theirs = (lambda o: ref["hawkes_kron"](state, ea, et, decay, KA, KE, o)) if ref else None
+                ms, host_us = _median_loop_ms(ours, name=f"hawkes.{kind}.N{N}")
+                line = {"workload": f"hawkes {kind}: N={N} streams, D={D} (128 assets x 8 types), fp32",
+                        "value": ms, "unit": "ms", "host_us_per_call": host_us, "gbs": nbytes / ms / 1e6,
+                        "frac_of_hbm": nbytes / ms / 1e6 / peaks["hbm_gbs"],
+                        "timing": "median of 7 x (100 back-to-back calls between two events)"}
+                if theirs is not None:
+                    o2 = torch.empty_like(state)
+                    ms_ref, _ = _median_loop_ms(lambda: theirs(o2))
+                    err = ((out.double() - o2.double()).norm() / o2.double().norm()).item()
+                    line.update({"reference_triton_ms": ms_ref, "speedup_vs_reference_triton": ms_ref / ms,
+                                 "rel_err_vs_reference": err})
+                else:
+                    line["reference_triton_ms"] = None
+                lines.append(line)
+    elif w == "pauli":
+        # The reference's Pauli-string Hamiltonian benchmark (pauli.py:1184-1300): K in {8, 12, 16, 20}
+        # qubits, S in {64, 256, 1024} strings, cases with 2^K S above 150 M skipped as it skips them;
+        # problems drawn by its make_problem. Its native_apply is timed at the partition count its
+        # tune_native picks (median_us: 5 repeats of a back-to-back loop); lsr.pauli.native_apply the
+        # same way. The state (at most 8 MB) stays in L2: the figure of merit is amplitude reads per
+        # second, 8 bytes per (output, string) pair.
+        from lsr import pauli as PA
+        ref = load_reference_module("pauli")
+        for K in (8, 12, 16, 20):
+            for S in (64, 256, 1024):
+                N = 1 << K
+                if N * S > 150_000_000:
+                    continue
+                if ref is not None:
+                    prob = ref.make_problem(K, S)
+                else:  # the same draw: seeded ops, coefficients / sqrt(S), a normalised random state
+                    gk = torch.Generator().manual_seed(17 + 10007 * K + S)
+                    ops = torch.randint(0, 4, (S, K), generator=gk, dtype=torch.int64)
+                    flip, sign, ny = PA.encode_pauli_strings(ops)
+                    coeff = torch.randn(S, generator=gk) / math.sqrt(S)
+                    pr, pi = torch.randn(N, generator=gk), torch.randn(N, generator=gk)
+                    nrm = torch.sqrt((pr ** 2).sum() + (pi ** 2).sum())
+                    prob = {"K": K, "S": S, "N": N, "flip": flip.to(dev), "sign": sign.to(dev), "ny": ny.to(dev),
+                            "coeff": coeff.to(dev), "psi_r": (pr / nrm).to(dev), "psi_i": (pi / nrm).to(dev)}
+                out_r, out_i = torch.empty(N, device=dev), torch.empty(N, device=dev)
+                iters = 100 if N * S <= 2_000_000 else (30 if N * S <= 20_000_000 else 10)
+                ms, host_us = _median_loop_ms(lambda: PA.native_apply(prob, 1, None, None, out_r, out_i),
+                                              warmup=3, iters=iters, repeats=5, name=f"pauli.K{K}.S{S}")
+                pairs = float(N) * S
+                line = {"workload": f"pauli: K={K} qubits (N={N}), S={S} strings, complex fp32", "value": ms,
+                        "unit": "ms", "host_us_per_call": host_us, "amplitude_reads_per_s": pairs / ms * 1e3,
+                        "timing": f"median of 5 x ({iters} back-to-back calls between two events)"}
+                if ref is not None:
+                    best, _ = ref.tune_native(prob)
+                    want = best["out_r"].double() + 1j * best["out_i"].double()
+                    got = out_r.double() + 1j * out_i.double()
+                    line.update({"reference_triton_ms": best["us"] / 1e3, "reference_P": best["P"],
+                                 "speedup_vs_reference_triton": best["us"] / 1e3 / ms,
+                                 "rel_err_vs_reference": ((got - want).abs().norm() / want.abs().norm()).item()})
+                else:
+                    line["reference_triton_ms"] = None
+                lines.append(line)
     elif w == "f1":
         # Batched coupled Newton inverse roots on the reference's full bucket list
         # (shampoo.py:812-840: (n, root, B), seeds 17 + 100 j, tolerance 1e-6,
@@ -1009,7 +1103,7 @@ def main(argv=None) -> int:
                     help="N>1: parameter exchange (peer-memory push or NCCL all-gather)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["muon", "cfg1", "cfg2", "cfg3", "cfg5", "cfg5s", "refresh", "f1", "muon_torch",
-                                           "kronrec",
+                                           "kronrec", "hawkes", "pauli",
                                            "kron64x8"],
                     default="muon",
                     help="muon = the headline GPT-2-XL Muon step (default); cfgN = per-row workloads")

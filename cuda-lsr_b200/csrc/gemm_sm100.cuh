@@ -379,30 +379,47 @@ __device__ __forceinline__ void aux_prefetch(const GroupDesc& G, int b, int row0
   }
 }
 
+// Adam moments of one 32 x 32 chunk for the EPI_SOAP_ADAM epilogue, held in
+// registers: lane l owns the 16-byte vectors (row (l / 8) + 4 i, columns 4 (l % 8)
+// .. + 3) for i < 8, so m and v move in coalesced 128-byte row segments. The
+// epilogue loads the NEXT live chunk's moments while it processes the current
+// one (512 bytes in flight per lane), which keeps the moment stream going while
+// the accumulator is read out, staged and the results stored. Empty for the
+// other epilogues.
+template <int EPI>
+struct MomentChunk {
+  __device__ __forceinline__ void load(const GroupDesc&, int, int, int, int) {}
+};
+
+template <>
+struct MomentChunk<EPI_SOAP_ADAM> {
+  float4 m[8], v[8];
+  __device__ __forceinline__ void load(const GroupDesc& G, int b, int row0, int col0, int lane) {
+    const int jv = lane & 7;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int gr = row0 + (lane >> 3) + 4 * i, gc = col0 + 4 * jv;
+      m[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (gr < G.M && gc < G.N) {
+        const long long idx = (long long)b * G.out_bs + (long long)gr * G.ldo + gc;
+        m[i] = __ldcs(reinterpret_cast<const float4*>(G.st_m + idx));
+        v[i] = __ldcs(reinterpret_cast<const float4*>(G.st_v + idx));
+      }
+    }
+  }
+};
+
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk_staged(const GemmParams& p, int g, const GroupDesc& G, int b,
                                                       int row0, int col0, int lane, const uint32_t (&r)[32],
                                                       const uint4 (&cur)[EpiT<EPI>::VPR], uint8_t* dbuf,
-                                                      uint8_t* tbuf) {
+                                                      uint8_t* tbuf, const MomentChunk<EPI>& mom) {
   using T = EpiT<EPI>;
   if constexpr (EPI == EPI_SOAP_ADAM) {
     // Work row-contiguously: 8 lanes per row, 16-byte vectors, so m / v / u move
-    // in coalesced segments. All eight rows' m and v loads of this lane are
-    // issued first (256 B in flight per lane), then the accumulator rows are
-    // staged, so the loads' latency overlaps the staging.
+    // in coalesced segments; this chunk's moments were loaded one chunk ahead.
     const int jv = lane & 7;
-    float4 mr[8], vr[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int gr = row0 + (lane >> 3) + 4 * i, gc = col0 + 4 * jv;
-      mr[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-      vr[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (gr < G.M && gc < G.N) {
-        const long long idx = (long long)b * G.out_bs + (long long)gr * G.ldo + gc;
-        mr[i] = *reinterpret_cast<const float4*>(G.st_m + idx);
-        vr[i] = *reinterpret_cast<const float4*>(G.st_v + idx);
-      }
-    }
     __syncwarp();  // the previous chunk's reads of dbuf are done
 #pragma unroll
     for (int j = 0; j < 8; ++j)
@@ -415,8 +432,8 @@ __device__ __forceinline__ void epilogue_chunk_staged(const GemmParams& p, int g
       if (gr >= G.M || gc >= G.N) continue;
       const float4 g4 = *reinterpret_cast<const float4*>(dbuf + stg_off<128>(rr, jv));
       const long long idx = (long long)b * G.out_bs + (long long)gr * G.ldo + gc;
-      float4 m4 = mr[i];
-      float4 v4 = vr[i];
+      const float4 m4 = mom.m[i];
+      const float4 v4 = mom.v[i];
       const float gg[4] = {g4.x, g4.y, g4.z, g4.w};
       float mm[4] = {m4.x, m4.y, m4.z, m4.w}, vv[4] = {v4.x, v4.y, v4.z, v4.w}, uu[4];
 #pragma unroll
@@ -425,8 +442,8 @@ __device__ __forceinline__ void epilogue_chunk_staged(const GemmParams& p, int g
         vv[e] = fmaf(G.b2, vv[e], (1.f - G.b2) * gg[e] * gg[e]);
         uu[e] = (mm[e] * G.c1) / (sqrtf(vv[e] * G.c2) + G.eps);
       }
-      *reinterpret_cast<float4*>(G.st_m + idx) = make_float4(mm[0], mm[1], mm[2], mm[3]);
-      *reinterpret_cast<float4*>(G.st_v + idx) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      __stcs(reinterpret_cast<float4*>(G.st_m + idx), make_float4(mm[0], mm[1], mm[2], mm[3]));
+      __stcs(reinterpret_cast<float4*>(G.st_v + idx), make_float4(vv[0], vv[1], vv[2], vv[3]));
       uint2 u2;
       __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u2);
       h[0] = __floats2bfloat162_rn(uu[0], uu[1]);
@@ -1056,6 +1073,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
       if constexpr (ET::AUX) {
         if (G.tma_out && live) aux_prefetch<EPI>(G, b, row0, tj * BN + (__ffs(live) - 1) * 32, lane, pre);
       }
+      MomentChunk<EPI> mom_next;
+      if constexpr (EPI == EPI_SOAP_ADAM) {
+        if (live) mom_next.load(G, b, row0, tj * BN + (__ffs(live) - 1) * 32, lane);
+      }
       if (!mbar_wait(tfull + acc, aph, abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t tbase =
@@ -1085,10 +1106,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
           if constexpr (ET::AUX) {
             if (rem) aux_prefetch<EPI>(G, b, row0, tj * BN + (__ffs(rem) - 1) * 32, lane, pre);
           }
+          const MomentChunk<EPI> mom = mom_next;
+          if constexpr (EPI == EPI_SOAP_ADAM) {
+            if (rem) mom_next.load(G, b, row0, tj * BN + (__ffs(rem) - 1) * 32, lane);
+          }
           tmem_ld_wait();
           uint8_t* dbuf = ebase + (kchunk & 1) * ET::CHB;
           uint8_t* tbuf = ebase + (2 + (kchunk & 1)) * ET::CHB;
-          epilogue_chunk_staged<EPI>(p, g, G, b, row0, col0, lane, r, cur, dbuf, tbuf);
+          epilogue_chunk_staged<EPI>(p, g, G, b, row0, col0, lane, r, cur, dbuf, tbuf, mom);
           ++kchunk;
         } else {
           tmem_ld_wait();

@@ -19,6 +19,8 @@
 // given to the tensor core K-major (MN-major tf32 operands read as zero on this
 // part): the split pass writes a transposed copy where a product needs one, and
 // the intermediate of a right-first apply is stored transposed by its epilogue.
+#include <atomic>
+
 #include "runtime.cuh"
 
 namespace lsr {
@@ -96,6 +98,20 @@ constexpr int kDenseMaxMN = 1024;
 bool kron_use_dense(int m, int n) {
   const long long mn = (long long)m * n;
   return mn <= kDenseMaxMN && mn % 4 == 0;
+}
+
+// Small fp32 problems (m <= 64, n in {1, 2, 4, 8, 16}, at most kSmallMaxFlop):
+// one FFMA launch with no workspace (kron_small_kernel). Here the tensor-core
+// paths are bound by latency, not by the math: the dense operator's GEMM has a
+// handful of 128 x 256 tiles, each walking 3 x (m n / 32) K blocks in series
+// (measured on the reference's x [M, 64, 8] sweep: a 31 us floor per call for
+// M <= 1024, against 2 (m n)(m + n) S M flops that take a few us on every SM).
+constexpr double kSmallMaxFlop = 1.0e9;
+constexpr int KS_THREADS = 256;
+
+bool kron_use_small(int batch, int m, int n, int nterms) {
+  if (m > 64 || n > 16 || 32 % n) return false;
+  return 2.0 * batch * nterms * m * n * (double)(m + n) <= kSmallMaxFlop;
 }
 
 // W[(i n + j)][(k n + l)] = sum_s A_s[i][k] B_s[j][l]  (A_s[i][k] = at[s][k][i] when a_trans),
@@ -232,6 +248,7 @@ size_t lsr_kron_apply_workspace_bytes(int batch, int m, int n, int nterms, int f
   if (!kron_dims_ok(batch, m, n, nterms)) return 0;
   const size_t mn = (size_t)batch * m * n;
   if (!f32) return 2 * a256(mn * 2) + 256;  // bf16 hi/lo intermediate
+  if (kron_use_small(batch, m, n, nterms)) return 0;  // one FFMA launch, no workspace
   if (kron_use_dense(m, n)) {
     const size_t w = (size_t)m * n * m * n * 4;
     return 2 * a256(w) + 2 * a256(mn * 4) + 256;  // W hi/lo, X hi/lo
@@ -425,6 +442,160 @@ int kron_apply_dense_f32(const void* A, int a_trans, const void* X, const void* 
   return rc ? rc : dense_apply(Wh, Wl, static_cast<const float*>(X), Y, batch, mn, Xh, Xl, st);
 }
 
+// Small Kronecker apply, fp32 FFMA: Y[b] = sum_s A_s X[b] B_s^T for X [batch][m][n].
+// A block takes NW / n right-hand sides (their X staged in shared memory once)
+// and all m <= 64 rows. Per term s it forms T = [X_0 B_s^T | ... ] (m x NW) in
+// shared memory and adds A_s T into a register tile (RI rows x CPT columns per
+// thread, NW = 16 CPT), so the sum over s stays in registers and Y is written
+// once. A_{s+1} and B_{s+1} are loaded into registers while term s computes
+// and stored into the other half of a double buffer, so no term waits for a
+// global load. Lanes 0-15 / 16-31 of a warp take adjacent column groups of two
+// row groups: every read of T is one wavefront and the A reads are broadcasts.
+constexpr int KS_MAXM = 64, KS_PRE = KS_MAXM * KS_MAXM / KS_THREADS;  // A_s elements per thread
+
+template <int RI, int CPT>
+__global__ void __launch_bounds__(KS_THREADS) kron_small_kernel(const float* __restrict__ A, int a_trans,
+                                                                const float* __restrict__ X,
+                                                                const float* __restrict__ B, float* __restrict__ Y,
+                                                                int batch, int m, int n, int S) {
+  extern __shared__ __align__(16) float ksm[];
+  constexpr int NW = 16 * CPT;
+  const int P = NW / n, xs = m * n + 1;  // padded per-snapshot stride: the P snapshots sit in distinct banks
+  const int mm = m * m, nn = n * n;
+  float* Xs = ksm;                       // [P][m n (+1)]
+  float* T = Xs + ((P * xs + 3) & ~3);   // [m][NW]
+  float* As = T + m * NW;                // [2][m (k)][m (i)]: As[k][i] = A_s[i][k]
+  float* Bs = As + 2 * mm;               // [2][n][n]
+  const int m0 = blockIdx.x * P;
+  const int np = min(P, batch - m0);
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int cg = lane & 15;              // column group: columns CPT cg ..
+  const int ig = (lane >> 4) + 2 * w;    // row group: rows RI ig ..
+  const long long xo = (long long)m0 * m * n;
+  for (int e = tid; e < P * m * n; e += KS_THREADS) {
+    const int p = e / (m * n), q = e - p * (m * n);
+    Xs[p * xs + q] = p < np ? X[xo + e] : 0.f;
+  }
+  // element e of As (k = e / m, i = e % m) from term s
+  auto a_elem = [&](int s, int e) -> float {
+    const int k = e / m, i = e - k * m;
+    const float* src = A + (size_t)s * mm;
+    return a_trans ? __ldg(src + e) : __ldg(src + (size_t)i * m + k);
+  };
+  for (int e = tid; e < mm; e += KS_THREADS) As[e] = a_elem(0, e);
+  for (int e = tid; e < nn; e += KS_THREADS) Bs[e] = __ldg(B + e);
+  float acc[RI][CPT];
+#pragma unroll
+  for (int r = 0; r < RI; ++r)
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) acc[r][c] = 0.f;
+  __syncthreads();
+  for (int s = 0; s < S; ++s) {
+    const int cur = s & 1;
+    const float* Ac = As + cur * mm;
+    const float* Bc = Bs + cur * nn;
+    float pre[KS_PRE], preb = 0.f;
+    const bool more = s + 1 < S;
+    if (more) {
+#pragma unroll
+      for (int q = 0; q < KS_PRE; ++q) {
+        const int e = tid + q * KS_THREADS;
+        pre[q] = e < mm ? a_elem(s + 1, e) : 0.f;
+      }
+      if (tid < nn) preb = __ldg(B + (size_t)(s + 1) * nn + tid);
+    }
+    for (int e = tid; e < m * NW; e += KS_THREADS) {
+      const int k = e / NW, c = e - k * NW, p = c / n, j = c - p * n;
+      const float* xr = Xs + p * xs + k * n;
+      const float* br = Bc + j * n;
+      float t = 0.f;
+      for (int l = 0; l < n; ++l) t = fmaf(xr[l], br[l], t);
+      T[e] = t;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int k = 0; k < m; ++k) {
+      float tv[CPT];
+      if constexpr (CPT == 2) {
+        const float2 t2 = *reinterpret_cast<const float2*>(T + k * NW + 2 * cg);
+        tv[0] = t2.x;
+        tv[1] = t2.y;
+      } else {
+        tv[0] = T[k * NW + cg];
+      }
+#pragma unroll
+      for (int r = 0; r < RI; ++r) {
+        const int i = ig * RI + r;
+        const float a = i < m ? Ac[k * m + i] : 0.f;
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) acc[r][c] = fmaf(a, tv[c], acc[r][c]);
+      }
+    }
+    if (more) {
+      float* An = As + (cur ^ 1) * mm;
+#pragma unroll
+      for (int q = 0; q < KS_PRE; ++q) {
+        const int e = tid + q * KS_THREADS;
+        if (e < mm) An[e] = pre[q];
+      }
+      if (tid < nn) Bs[(cur ^ 1) * nn + tid] = preb;
+    }
+    __syncthreads();  // T read by every thread; the next term's A / B stored
+  }
+#pragma unroll
+  for (int r = 0; r < RI; ++r) {
+    const int i = ig * RI + r;
+    if (i >= m) continue;
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) {
+      const int col = CPT * cg + c, p = col / n, j = col - p * n;
+      if (p < np) Y[((long long)(m0 + p) * m + i) * n + j] = acc[r][c];
+    }
+  }
+}
+
+template <int RI, int CPT>
+int launch_small(const float* A, int a_trans, const float* X, const float* B, float* Y, int batch, int m, int n,
+                 int S, cudaStream_t st) {
+  static std::atomic<int> attr_set{0};
+  constexpr int NW = 16 * CPT;
+  const int P = NW / n;
+  const size_t smem =
+      ((size_t)((P * (m * n + 1) + 3) & ~3) + (size_t)m * NW + 2 * (size_t)m * m + 2 * (size_t)n * n) * 4;
+  constexpr int kMaxSmem = 64 * 1024;  // m <= 64, n <= 16: at most 32 (64 + 1) + 64 x 32 + 2 (4096 + 256) floats
+  if (smem > (size_t)kMaxSmem) return LSR_ERR_SHAPE;
+  if (!attr_set.load(std::memory_order_relaxed)) {
+    if (cudaFuncSetAttribute(kron_small_kernel<RI, CPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
+        cudaSuccess)
+      return LSR_ERR_LAUNCH;
+    attr_set.store(1, std::memory_order_relaxed);
+  }
+  ProfScope prof(PK_GEMM_OTHER, st);
+  kron_small_kernel<RI, CPT><<<cdiv(batch, P), KS_THREADS, smem, st>>>(A, a_trans, X, B, Y, batch, m, n, S);
+  return launch_ok();
+}
+
+// 32-column blocks (two columns per thread) once there are enough right-hand sides
+// to give every SM two blocks; 16-column blocks below that, so small batches
+// still spread over the GPU. RI = rows per thread = m / 16, rounded up.
+template <int CPT>
+int small_rows(const float* A, int a_trans, const float* X, const float* B, float* Y, int batch, int m, int n, int S,
+               cudaStream_t st) {
+  switch (cdiv(m, 16)) {
+    case 1: return launch_small<1, CPT>(A, a_trans, X, B, Y, batch, m, n, S, st);
+    case 2: return launch_small<2, CPT>(A, a_trans, X, B, Y, batch, m, n, S, st);
+    case 3: return launch_small<3, CPT>(A, a_trans, X, B, Y, batch, m, n, S, st);
+    default: return launch_small<4, CPT>(A, a_trans, X, B, Y, batch, m, n, S, st);
+  }
+}
+
+int kron_apply_small_f32(const float* A, int a_trans, const float* X, const float* B, float* Y, int batch, int m,
+                         int n, int S, cudaStream_t st) {
+  if (n <= 16 && 16 % n == 0 && cdiv(batch, 16 / n) < 2 * device_sm_count())
+    return small_rows<1>(A, a_trans, X, B, Y, batch, m, n, S, st);
+  return small_rows<2>(A, a_trans, X, B, Y, batch, m, n, S, st);
+}
+
 int kron_apply(const void* A, int a_trans, const void* X, const void* B, float* Y, int batch, int m, int n,
                int nterms, int f32, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (!kron_dims_ok(batch, m, n, nterms)) return LSR_ERR_ARG;
@@ -432,6 +603,9 @@ int kron_apply(const void* A, int a_trans, const void* X, const void* B, float* 
   if (!A || !X || !B || !Y) return LSR_ERR_ARG;
   int rc = check_device();
   if (rc) return rc;
+  if (f32 && kron_use_small(batch, m, n, nterms))
+    return kron_apply_small_f32(static_cast<const float*>(A), a_trans, static_cast<const float*>(X),
+                                static_cast<const float*>(B), Y, batch, m, n, nterms, st);
   if (!ws || ws_bytes < lsr_kron_apply_workspace_bytes(batch, m, n, nterms, f32)) return LSR_ERR_WORKSPACE;
   uint8_t* w = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(ws), 256));
   const size_t mn = (size_t)batch * m * n;
@@ -556,60 +730,88 @@ int lsr_kron_apply_f32(const float* A, int a_trans, const float* X, const float*
 // Tiny-factor Kronecker reconstruction  W = sum_s F_0[s] ⊗ F_1[s] ⊗ ... ⊗ F_{K-1}[s]
 //
 // Replaces direct_k{3,4,5}_kernel / native_reconstruct (kron_cuda.py:242-583):
-// one thread per entry W[i][j]; (i, j) are decoded into mixed-radix mode
-// digits, one scalar is read from every factor and the K scalars multiplied,
-// accumulated over s in order; no partial Kronecker product is materialised.
-// Every factor (a few KB for the reference's 16 x 768 cases) is staged once
-// per block in shared memory. The work is a single wave of a few dozen
-// blocks: latency-bound, not bandwidth- or compute-bound.
+// each output entry W[i][j] is decoded into mixed-radix mode digits once, one
+// scalar is read from every factor per term and the K scalars multiplied; no
+// partial Kronecker product is materialised. The kernel is specialised on K
+// (unrolled factor loop, factor pointers and extents in registers). A block
+// covers 64 consecutive entries and splits the S terms into 4 contiguous
+// slices, one per 64-thread group, summed in a fixed order at the end (the
+// result does not depend on scheduling): 16 x 768 outputs make 192 blocks, so
+// every SM works even at S = 256. Factors are read through the read-only
+// cache; the reference's largest factor set (K = 3, S = 256) is 213 KB.
 // ---------------------------------------------------------------------------
 
 namespace lsr {
 namespace {
 
 constexpr int kMaxFactors = 8;
+constexpr int REC_OUTS = 64, REC_SPLIT = 4;
 
 struct RecParams {
   const float* f[kMaxFactors];
   int r[kMaxFactors], c[kMaxFactors];
-  int off[kMaxFactors];  // offset of factor k in the staged buffer (floats)
-  int K, S;
+  int S;
   long long R, C;
-  int staged;  // factors fit in shared memory
 };
 
-__global__ void __launch_bounds__(256) kron_reconstruct_kernel(RecParams p, float* __restrict__ W) {
-  extern __shared__ float sf[];
-  if (p.staged) {
-    for (int k = 0; k < p.K; ++k) {
-      const int n = p.S * p.r[k] * p.c[k];
-      for (int i = threadIdx.x; i < n; i += blockDim.x) sf[p.off[k] + i] = p.f[k][i];
+template <int K>
+__global__ void __launch_bounds__(REC_OUTS * REC_SPLIT) kron_reconstruct_kernel(const __grid_constant__ RecParams p,
+                                                                               float* __restrict__ W) {
+  __shared__ float part[REC_SPLIT][REC_OUTS];
+  const int o = threadIdx.x % REC_OUTS, q = threadIdx.x / REC_OUTS;
+  const long long total = p.R * p.C;
+  const float* f[K];
+  int sz[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    f[k] = p.f[k];
+    sz[k] = p.r[k] * p.c[k];
+  }
+  const int s0 = (int)((long long)p.S * q / REC_SPLIT), s1 = (int)((long long)p.S * (q + 1) / REC_SPLIT);
+  for (long long base = (long long)blockIdx.x * REC_OUTS; base < total; base += (long long)gridDim.x * REC_OUTS) {
+    const long long e = base + o;
+    float acc = 0.f;
+    if (e < total) {
+      long long i = e / p.C, j = e - (e / p.C) * p.C;
+      const float* ptr[K];
+#pragma unroll
+      for (int k = K - 1; k >= 0; --k) {  // the last factor is the fastest-varying mode
+        const int ik = (int)(i % p.r[k]), jk = (int)(j % p.c[k]);
+        i /= p.r[k];
+        j /= p.c[k];
+        ptr[k] = f[k] + (long long)s0 * sz[k] + ik * p.c[k] + jk;
+      }
+#pragma unroll 4
+      for (int s = s0; s < s1; ++s) {
+        float prod = __ldg(ptr[0]);
+        ptr[0] += sz[0];
+#pragma unroll
+        for (int k = 1; k < K; ++k) {
+          prod *= __ldg(ptr[k]);
+          ptr[k] += sz[k];
+        }
+        acc += prod;
+      }
+    }
+    part[q][o] = acc;
+    __syncthreads();
+    if (q == 0 && e < total) {
+      float w = part[0][o];
+#pragma unroll
+      for (int k = 1; k < REC_SPLIT; ++k) w += part[k][o];
+      W[e] = w;
     }
     __syncthreads();
   }
+}
+
+template <int K>
+int launch_reconstruct(const RecParams& p, float* W, cudaStream_t st) {
   const long long total = p.R * p.C;
-  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
-       e += (long long)gridDim.x * blockDim.x) {
-    long long i = e / p.C, j = e - (e / p.C) * p.C;
-    int idx[kMaxFactors];
-    for (int k = p.K - 1; k >= 0; --k) {  // last factor is the fastest-varying mode
-      const int ik = (int)(i % p.r[k]), jk = (int)(j % p.c[k]);
-      i /= p.r[k];
-      j /= p.c[k];
-      idx[k] = ik * p.c[k] + jk;
-    }
-    float acc = 0.f;
-    for (int s = 0; s < p.S; ++s) {
-      float prod = 1.f;
-      for (int k = 0; k < p.K; ++k) {
-        const int sz = p.r[k] * p.c[k];
-        const float v = p.staged ? sf[p.off[k] + s * sz + idx[k]] : __ldg(p.f[k] + (long long)s * sz + idx[k]);
-        prod = (k == 0) ? v : prod * v;
-      }
-      acc += prod;
-    }
-    W[e] = acc;
-  }
+  const int blocks = (int)std::max<long long>(
+      1, std::min<long long>((total + REC_OUTS - 1) / REC_OUTS, 8LL * lsr::device_sm_count()));
+  kron_reconstruct_kernel<K><<<blocks, REC_OUTS * REC_SPLIT, 0, st>>>(p, W);
+  return cudaGetLastError() == cudaSuccess ? LSR_OK : LSR_ERR_LAUNCH;
 }
 
 }  // namespace
@@ -621,36 +823,32 @@ int lsr_kron_reconstruct_f32(const float* const* factors, const int* rows, const
                              lsr_stream_t stream) {
   if (!factors || !rows || !cols || !W || K < 1 || K > lsr::kMaxFactors || S < 0) return LSR_ERR_ARG;
   lsr::RecParams p{};
-  p.K = K;
   p.S = S;
   p.R = 1;
   p.C = 1;
-  long long staged_floats = 0;
   for (int k = 0; k < K; ++k) {
     if (!factors[k] || rows[k] <= 0 || cols[k] <= 0) return LSR_ERR_ARG;
     p.f[k] = factors[k];
     p.r[k] = rows[k];
     p.c[k] = cols[k];
-    p.off[k] = (int)staged_floats;
-    staged_floats += (long long)S * rows[k] * cols[k];
     p.R *= rows[k];
     p.C *= cols[k];
-    if (p.R > (1LL << 31) || p.C > (1LL << 31)) return LSR_ERR_SHAPE;
+    if (p.R > (1LL << 31) || p.C > (1LL << 31) || (long long)rows[k] * cols[k] > (1LL << 31)) return LSR_ERR_SHAPE;
   }
   int rc = lsr::check_device();
   if (rc) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const size_t smem = (size_t)staged_floats * 4;
-  p.staged = smem <= 160 * 1024;
-  auto kfn = lsr::kron_reconstruct_kernel;
-  if (p.staged && smem > 48 * 1024 &&
-      cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return LSR_ERR_LAUNCH;
-  const long long total = p.R * p.C;
-  const int blocks = (int)std::max<long long>(1, std::min<long long>((total + 255) / 256, 4LL * lsr::device_sm_count()));
   lsr::ProfScope prof(lsr::PK_EW_OTHER, st);
-  kfn<<<blocks, 256, p.staged ? smem : 0, st>>>(p, W);
-  return cudaGetLastError() == cudaSuccess ? LSR_OK : LSR_ERR_LAUNCH;
+  switch (K) {
+    case 1: return lsr::launch_reconstruct<1>(p, W, st);
+    case 2: return lsr::launch_reconstruct<2>(p, W, st);
+    case 3: return lsr::launch_reconstruct<3>(p, W, st);
+    case 4: return lsr::launch_reconstruct<4>(p, W, st);
+    case 5: return lsr::launch_reconstruct<5>(p, W, st);
+    case 6: return lsr::launch_reconstruct<6>(p, W, st);
+    case 7: return lsr::launch_reconstruct<7>(p, W, st);
+    default: return lsr::launch_reconstruct<8>(p, W, st);
+  }
 }
 
 }  // extern "C"

@@ -79,6 +79,141 @@ __device__ __forceinline__ void qr_block_sum32(float (&acc)[32], float* red, flo
   __syncthreads();
 }
 
+// Block-reflector update of column pairs of a trailing matrix C (m rows, row
+// stride n): C -= V X (V^T C), X = T^T (factorization: H_1 ... H_w applied
+// transposed) or X = T (forming Q). V is the panel in shared memory: unit
+// lower-trapezoidal, V[i][k] = P[i][k] for i > k, 1 on the diagonal, 0 above.
+// Each thread owns columns c and c + QR_THREADS, so every broadcast read of a
+// V row feeds two FMA chains; the rows below the 32-row triangle go in
+// batches of QR_ROWB, their loads issued together (the matrix streams from L2 /
+// DRAM: one load in flight per thread would leave the kernel latency-bound).
+constexpr int QR_ROWB = 8;
+
+template <bool TRANS_T>
+__device__ __forceinline__ void wy_update_cols(float* C, int n, int m, int ncols, int w, const float* P,
+                                               const float* Ts) {
+  for (int c0 = threadIdx.x; c0 < ncols; c0 += 2 * QR_THREADS) {
+    const int c1 = c0 + QR_THREADS;
+    const bool has1 = c1 < ncols;
+    float* col0 = C + c0;
+    float* col1 = C + (has1 ? c1 : c0);
+    float a0[32], a1[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) a0[k] = a1[k] = 0.f;
+    const int mt = min(m, QR_NB);
+    for (int i = 0; i < mt; ++i) {  // the triangle
+      const float x0 = col0[(size_t)i * n], x1 = col1[(size_t)i * n];
+      const float* row = P + i * QR_LDP;
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const float v = k < i ? row[k] : (k == i ? 1.f : 0.f);
+        a0[k] = fmaf(v, x0, a0[k]);
+        a1[k] = fmaf(v, x1, a1[k]);
+      }
+    }
+    int i = mt;
+    for (; i + QR_ROWB <= m; i += QR_ROWB) {
+      float x0[QR_ROWB], x1[QR_ROWB];
+#pragma unroll
+      for (int u = 0; u < QR_ROWB; ++u) {
+        x0[u] = col0[(size_t)(i + u) * n];
+        x1[u] = col1[(size_t)(i + u) * n];
+      }
+#pragma unroll
+      for (int u = 0; u < QR_ROWB; ++u) {
+        const float* row = P + (i + u) * QR_LDP;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const float v = row[k];
+          a0[k] = fmaf(v, x0[u], a0[k]);
+          a1[k] = fmaf(v, x1[u], a1[k]);
+        }
+      }
+    }
+    for (; i < m; ++i) {
+      const float x0 = col0[(size_t)i * n], x1 = col1[(size_t)i * n];
+      const float* row = P + i * QR_LDP;
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        a0[k] = fmaf(row[k], x0, a0[k]);
+        a1[k] = fmaf(row[k], x1, a1[k]);
+      }
+    }
+    // y = X a in place (T upper triangular): T^T a needs a[0..k] for y[k], so
+    // k runs downwards; T a needs a[k..31], so k runs upwards
+    if (TRANS_T) {
+#pragma unroll
+      for (int k = 31; k >= 0; --k) {
+        float t0 = 0.f, t1 = 0.f;
+#pragma unroll
+        for (int r = 0; r <= k; ++r) {
+          t0 = fmaf(Ts[r * QR_LDP + k], a0[r], t0);
+          t1 = fmaf(Ts[r * QR_LDP + k], a1[r], t1);
+        }
+        a0[k] = k < w ? t0 : 0.f;
+        a1[k] = k < w ? t1 : 0.f;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        float t0 = 0.f, t1 = 0.f;
+#pragma unroll
+        for (int r = k; r < 32; ++r) {
+          t0 = fmaf(Ts[k * QR_LDP + r], a0[r], t0);
+          t1 = fmaf(Ts[k * QR_LDP + r], a1[r], t1);
+        }
+        a0[k] = k < w ? t0 : 0.f;
+        a1[k] = k < w ? t1 : 0.f;
+      }
+    }
+    // C[i] -= sum_k V[i][k] y[k]
+    for (int r = 0; r < mt; ++r) {
+      const float* row = P + r * QR_LDP;
+      float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const float v = k < r ? row[k] : (k == r ? 1.f : 0.f);
+        d0 = fmaf(v, a0[k], d0);
+        d1 = fmaf(v, a1[k], d1);
+      }
+      col0[(size_t)r * n] -= d0;
+      if (has1) col1[(size_t)r * n] -= d1;
+    }
+    int r = mt;
+    for (; r + QR_ROWB <= m; r += QR_ROWB) {
+      float x0[QR_ROWB], x1[QR_ROWB];
+#pragma unroll
+      for (int u = 0; u < QR_ROWB; ++u) {
+        x0[u] = col0[(size_t)(r + u) * n];
+        x1[u] = col1[(size_t)(r + u) * n];
+      }
+#pragma unroll
+      for (int u = 0; u < QR_ROWB; ++u) {
+        const float* row = P + (r + u) * QR_LDP;
+        float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          d0 = fmaf(row[k], a0[k], d0);
+          d1 = fmaf(row[k], a1[k], d1);
+        }
+        col0[(size_t)(r + u) * n] = x0[u] - d0;
+        if (has1) col1[(size_t)(r + u) * n] = x1[u] - d1;
+      }
+    }
+    for (; r < m; ++r) {
+      const float* row = P + r * QR_LDP;
+      float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        d0 = fmaf(row[k], a0[k], d0);
+        d1 = fmaf(row[k], a1[k], d1);
+      }
+      col0[(size_t)r * n] -= d0;
+      if (has1) col1[(size_t)r * n] -= d1;
+    }
+  }
+}
+
 // A [b][n][n] (row-major) is factored in place: R on and above the diagonal,
 // the Householder vectors (unit leading entry implied) below it; tau [b][n];
 // T [b][P][32][32] the upper-triangular WY factor of each panel.
@@ -153,41 +288,8 @@ __global__ void __launch_bounds__(QR_THREADS, 1) qr_factor_kernel(float* A, floa
     }
     for (int idx = tid; idx < QR_NB * QR_NB; idx += QR_THREADS)
       T[((size_t)b * npan + p) * QR_NB * QR_NB + idx] = Ts[(idx / QR_NB) * QR_LDP + idx % QR_NB];
-    // trailing matrix: A2 (rows c0.., cols c0+w..) -= V T^T (V^T A2), one thread per column
-    const int nc = n - c0 - w;
-    for (int cc = tid; cc < nc; cc += QR_THREADS) {
-      float* col = Ab + (size_t)c0 * n + c0 + w + cc;
-      float acc[32];
-#pragma unroll
-      for (int k = 0; k < 32; ++k) acc[k] = 0.f;
-      for (int i = 0; i < m; ++i) {
-        const float a = col[(size_t)i * n];
-        const float* row = P + i * QR_LDP;
-#pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const float v = k < i ? row[k] : (k == i ? 1.f : 0.f);
-          acc[k] = fmaf(v, a, acc[k]);
-        }
-      }
-      float y[32];
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {  // y = T^T acc (T upper triangular)
-        float t = 0.f;
-#pragma unroll
-        for (int r = 0; r <= k; ++r) t = fmaf(Ts[r * QR_LDP + k], acc[r], t);
-        y[k] = k < w ? t : 0.f;
-      }
-      for (int i = 0; i < m; ++i) {
-        const float* row = P + i * QR_LDP;
-        float d = 0.f;
-#pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const float v = k < i ? row[k] : (k == i ? 1.f : 0.f);
-          d = fmaf(v, y[k], d);
-        }
-        col[(size_t)i * n] -= d;
-      }
-    }
+    // trailing matrix: A2 (rows c0.., cols c0+w..) -= V T^T (V^T A2)
+    wy_update_cols<true>(Ab + (size_t)c0 * n + c0 + w, n, m, n - c0 - w, w, P, Ts);
     __syncthreads();
   }
 }
@@ -214,39 +316,7 @@ __global__ void __launch_bounds__(QR_THREADS, 1) qr_form_q_kernel(const float* A
       Ts[(idx / QR_NB) * QR_LDP + idx % QR_NB] = T[((size_t)b * npan + p) * QR_NB * QR_NB + idx];
     __syncthreads();
     // Q2 (rows c0.., cols c0..) -= V T (V^T Q2)
-    for (int cc = tid; cc < m; cc += QR_THREADS) {
-      float* col = Qb + (size_t)c0 * n + c0 + cc;
-      float acc[32];
-#pragma unroll
-      for (int k = 0; k < 32; ++k) acc[k] = 0.f;
-      for (int i = 0; i < m; ++i) {
-        const float a = col[(size_t)i * n];
-        const float* row = P + i * QR_LDP;
-#pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const float v = k < i ? row[k] : (k == i ? 1.f : 0.f);
-          acc[k] = fmaf(v, a, acc[k]);
-        }
-      }
-      float y[32];
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {  // y = T acc (T upper triangular)
-        float t = 0.f;
-#pragma unroll
-        for (int r = k; r < 32; ++r) t = fmaf(Ts[k * QR_LDP + r], acc[r], t);
-        y[k] = k < w ? t : 0.f;
-      }
-      for (int i = 0; i < m; ++i) {
-        const float* row = P + i * QR_LDP;
-        float d = 0.f;
-#pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const float v = k < i ? row[k] : (k == i ? 1.f : 0.f);
-          d = fmaf(v, y[k], d);
-        }
-        col[(size_t)i * n] -= d;
-      }
-    }
+    wy_update_cols<false>(Qb + (size_t)c0 * n + c0, n, m, m, w, P, Ts);
     __syncthreads();
   }
   for (int c = tid; c < n; c += QR_THREADS) {

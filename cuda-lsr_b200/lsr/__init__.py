@@ -8,6 +8,8 @@ Drop-in Python surface over liblsr.so (include/lsr.h):
 * ``lsr.newton`` — coupled Newton inverse roots (coupled_newton_one,
   per_factor / batched / hybrid_coupled_newton).
 * ``lsr.dist``  — ShardedMuon across the GPUs of one node.
+* ``lsr.hawkes`` — multivariate Hawkes event update (hawkes_dense / hawkes_kron).
+* ``lsr.lm_driver`` — the language-model driver with the reference's command line.
 
 The CUDA library is loaded lazily on the first call; there is no CPU fallback.
 """

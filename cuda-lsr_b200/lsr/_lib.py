@@ -6,6 +6,7 @@ calls raise.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 import threading
@@ -87,6 +88,11 @@ SIGNATURES: dict[str, tuple] = {
     "lsr_kron_reconstruct_f32": (
         c_int, [ctypes.POINTER(c_void_p), ctypes.POINTER(c_int), ctypes.POINTER(c_int), c_int, c_int, c_void_p,
                 c_void_p]),
+    "lsr_hawkes_dense_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "lsr_hawkes_kron_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                    c_int, c_int, c_void_p]),
+    "lsr_pauli_apply_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                    c_int, c_int, c_void_p]),
     "lsr_soap_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "lsr_soap_direction_bf16": (
         c_int,
@@ -177,8 +183,25 @@ def check(rc: int, what: str) -> None:
         raise _ERRORS.get(rc, RuntimeError)(f"{what}: {msg} (liblsr code {rc})")
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_get_device = getattr(torch._C, "_cuda_getDevice", None)
+
+
 def stream_handle(device: torch.device | None = None) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """cudaStream_t of torch's current stream on `device` (the current device when None or unindexed)."""
+    if _raw_stream is None or _get_device is None:
+        return torch.cuda.current_stream(device).cuda_stream
+    idx = device.index if device is not None and device.index is not None else _get_device()
+    return _raw_stream(idx)
+
+
+def on_device(device: torch.device | int):
+    """Context that makes `device` the current CUDA device; costs nothing when it already is."""
+    if isinstance(device, int):
+        device = torch.device("cuda", device)
+    if device.index is None or (_get_device is not None and device.index == _get_device()):
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 def device_status(clear: bool = True) -> int:

@@ -65,7 +65,7 @@ class IpcBuffer:
         lib = _lib.load()
         ptr = ctypes.c_void_p()
         handle = (ctypes.c_ubyte * 64)()
-        with torch.cuda.device(device):
+        with _lib.on_device(device):
             _lib.check(lib.lsr_ipc_alloc(nbytes, ctypes.byref(ptr), handle), "lsr_ipc_alloc")
         self.ptr = int(ptr.value)
         self.nbytes = nbytes
@@ -109,7 +109,7 @@ class PeerExchange:
                 # peers listed from rank + 1 on: at any moment the ranks store into distinct receivers
                 for q in [(rank + k) % world for k in range(1, world)]:
                     p = ctypes.c_void_p()
-                    with torch.cuda.device(device):
+                    with _lib.on_device(device):
                         _lib.check(lib.lsr_ipc_open(handles[q][i], ctypes.byref(p)), "lsr_ipc_open")
                     row.append(int(p.value))
                 self.mapped.append(row)

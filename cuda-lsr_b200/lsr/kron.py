@@ -49,7 +49,7 @@ def kron_sum(A: torch.Tensor, X: torch.Tensor, B: torch.Tensor, out: torch.Tenso
     if Y.dtype != torch.float32 or not Y.is_contiguous() or Y.numel() != X3.numel():
         raise RuntimeError("out must be a contiguous float32 tensor shaped like X")
     lib = _lib.load()
-    with torch.cuda.device(X.device):
+    with _lib.on_device(X.device):
         st = _lib.stream_handle(X.device)
         if X.dtype == torch.bfloat16:
             rc = lib.lsr_kron_sum_bf16(A.data_ptr(), X3.data_ptr(), B.data_ptr(), Y.data_ptr(), batch, m, n, st)
@@ -92,8 +92,15 @@ def _kron_apply(X3, A3, B3, a_trans: bool, Y) -> None:
     S = A3.shape[0]
     f32 = X3.dtype == torch.float32
     lib = _lib.load()
+    nb = lib.lsr_kron_apply_workspace_bytes(batch, m, n, S, int(f32))
+    if f32 and nb == 0:  # small problem: one FFMA launch inside liblsr, no workspace
+        with _lib.on_device(X3.device):
+            rc = lib.lsr_kron_apply_f32(A3.data_ptr(), int(a_trans), X3.data_ptr(), B3.data_ptr(), Y.data_ptr(),
+                                        batch, m, n, S, None, 0, _lib.stream_handle(X3.device))
+        _lib.check(rc, "lsr_kron_apply")
+        return
     if f32 and m * n <= _DENSE_MAX_MN and (m * n) % 4 == 0:
-        with torch.cuda.device(X3.device):
+        with _lib.on_device(X3.device):
             Wh, Wl, _, _ = _dense_operator(A3, B3, a_trans)
             nb = lib.lsr_kron_dense_apply_workspace_bytes(batch, m * n)
             ws = _lib.WORKSPACE.get(nb, X3.device)
@@ -101,8 +108,7 @@ def _kron_apply(X3, A3, B3, a_trans: bool, Y) -> None:
                                                     m * n, ws.data_ptr(), nb, _lib.stream_handle(X3.device)),
                        "lsr_kron_dense_apply_f32")
         return
-    with torch.cuda.device(X3.device):
-        nb = lib.lsr_kron_apply_workspace_bytes(batch, m, n, S, int(f32))
+    with _lib.on_device(X3.device):
         ws = _lib.WORKSPACE.get(nb, X3.device)
         fn = lib.lsr_kron_apply_f32 if f32 else lib.lsr_kron_apply_bf16
         rc = fn(A3.data_ptr(), int(a_trans), X3.data_ptr(), B3.data_ptr(), Y.data_ptr(), batch, m, n, S,
@@ -185,7 +191,7 @@ def native_reconstruct(factors, K, out=None, block=256):
     rr = (ctypes.c_int * K)(*rows)
     cc = (ctypes.c_int * K)(*cols)
     lib = _lib.load()
-    with torch.cuda.device(out.device):
+    with _lib.on_device(out.device):
         rc = lib.lsr_kron_reconstruct_f32(ptrs, rr, cc, K, S, out.data_ptr(), _lib.stream_handle(out.device))
     _lib.check(rc, "lsr_kron_reconstruct_f32")
     return out

@@ -54,7 +54,7 @@ def _ns_call(X: torch.Tensor, ns_steps: int, eps: float, orient: bool, coef=(NS_
     if batch == 0 or Xb.numel() == 0:
         return out
     lib = _lib.load()
-    with torch.cuda.device(Xb.device):
+    with _lib.on_device(Xb.device):
         ws_bytes = lib.lsr_ns_workspace_bytes(batch, rows, cols, int(orient))
         ws = _lib.WORKSPACE.get(ws_bytes, Xb.device)
         rc = lib.lsr_ns_bf16(Xb.data_ptr(), out.data_ptr(), batch, rows, cols, int(orient), int(ns_steps),
@@ -155,7 +155,7 @@ class MuonStepEngine:
         dev = items[0][0].device
         arr, keep = self.make_groups(self.group_items(items))
         lib = _lib.load()
-        with torch.cuda.device(dev):
+        with _lib.on_device(dev):
             ws_bytes = lib.lsr_muon_workspace_bytes(arr, len(arr))
             ws = _lib.WORKSPACE.get(ws_bytes, dev)
             rc = lib.lsr_muon_step_bf16(arr, len(arr), float(momentum), int(bool(nesterov)), float(weight_decay),
@@ -178,7 +178,7 @@ class MuonStepEngine:
                 out.append(torch.empty(len(its), min(r, c), max(r, c), dtype=torch.bfloat16, device=dev))
         ptrs = (ctypes.c_void_p * len(out))(*[o.data_ptr() for o in out])
         lib = _lib.load()
-        with torch.cuda.device(dev):
+        with _lib.on_device(dev):
             ws_bytes = lib.lsr_muon_workspace_bytes(arr, len(arr))
             ws = _lib.WORKSPACE.get(ws_bytes, dev)
             rc = lib.lsr_muon_orthogonalize_bf16(arr, len(arr), float(momentum), int(bool(nesterov)), int(ns_steps),
@@ -202,7 +202,7 @@ class MuonStepEngine:
         dev = grouped[0][2][0][0].device
         arr, keep = self.make_groups(grouped)
         ptrs = (ctypes.c_void_p * len(out))(*[o.data_ptr() for o in out])
-        with torch.cuda.device(dev):
+        with _lib.on_device(dev):
             rc = _lib.load().lsr_muon_orthogonalize_phase_bf16(
                 arr, len(arr), float(momentum), int(bool(nesterov)), int(ns_steps), float(coef[0]), float(coef[1]),
                 float(coef[2]), float(eps), ptrs, int(phase), workspace.data_ptr(), workspace.numel(),
@@ -221,7 +221,7 @@ class MuonStepEngine:
                     len(its), min(shape), max(shape)):
                 raise ValueError("updates must be contiguous bf16 [count, min(r,c), max(r,c)] per group")
         ptrs = (ctypes.c_void_p * len(updates))(*[u.data_ptr() for u in updates])
-        with torch.cuda.device(dev):
+        with _lib.on_device(dev):
             rc = _lib.load().lsr_muon_apply_bf16(arr, len(arr), ptrs, float(weight_decay), float(base_lr),
                                                  _lib.stream_handle(dev))
         _lib.check(rc, "lsr_muon_apply_bf16")

@@ -8,8 +8,9 @@
  *   - nothing allocates: scratch memory comes from the caller's workspace
  *     (`ws`, `ws_bytes`), sized by the matching *_workspace_bytes() query;
  *   - the return value is LSR_OK or a negative LSR_ERR_* code; device-side
- *     failures (a bounded wait that timed out) are recorded in the library's
- *     device status word, read with lsr_device_status();
+ *     failures (a bounded wait that timed out: codes 101-107; an event index
+ *     out of range: 110) are recorded in the library's device status word,
+ *     read with lsr_device_status();
  *   - calls are thread-safe as long as concurrent calls use distinct
  *     workspaces.
  *
@@ -259,6 +260,9 @@ LSR_API int lsr_kron_sum_f32(const float* A, const float* X, const float* B, flo
  * Each term is two chained GEMMs (the cheaper association first); the
  * intermediate is kept as a hi + lo pair so the second product stays at fp32
  * accuracy.  _bf16: bf16 operands.  _f32: fp32 operands (3xTF32).
+ * Small fp32 problems (m <= 64, n in {1, 2, 4, 8, 16}, at most 1e9 flops, e.g.
+ * the reference's x [M, 64, 8] sweep up to M S ~ 13000) run as one fp32 FFMA
+ * launch instead: the workspace size is then 0 and ws may be NULL.
  * ---------------------------------------------------------------------- */
 LSR_API size_t lsr_kron_apply_workspace_bytes(int batch, int m, int n, int nterms, int f32);
 /* Small-factor Kronecker apply split in two, for callers that apply the same
@@ -289,6 +293,38 @@ LSR_API int lsr_kron_apply_f32(const float* A, int a_trans, const float* X, cons
  * ---------------------------------------------------------------------- */
 LSR_API int lsr_kron_reconstruct_f32(const float* const* factors, const int* rows, const int* cols, int K, int S,
                                      float* W, lsr_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Multivariate Hawkes event update, fp32, state [n][D] row-major:
+ *   dense: out[i][j] = decay[i] state[i][j] + kcol[event[i]][j]
+ *          (kcol = K^T, [D][D], so the selected column is contiguous);
+ *   kron : out[i][j] = decay[i] state[i][j] + ka[j / ne][event_asset[i]] ke[j % ne][event_type[i]]
+ *          (K = ka ⊗ ke, D = na ne, never formed).
+ * Events are int32. An event index out of range is not read: that stream's row
+ * is written as NaN and status 110 is recorded in the device status word.
+ * out may alias state (in-place update).
+ * Replaces hawkes_dense / hawkes_kron and their Triton kernels (hft.py:412-611).
+ * ---------------------------------------------------------------------- */
+LSR_API int lsr_hawkes_dense_f32(const float* state, const int* event, const float* decay, const float* kcol,
+                                 float* out, int n, int d, lsr_stream_t stream);
+LSR_API int lsr_hawkes_kron_f32(const float* state, const int* event_asset, const int* event_type,
+                                const float* decay, const float* ka, const float* ke, float* out, int n, int na,
+                                int ne, lsr_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Pauli-string Hamiltonian applied to a state vector of N = 2^K amplitudes,
+ * without forming H:
+ *   out[r] = sum_s coeff[s] i^{ny[s]} (-1)^{popcount((r ^ flip[s]) & sign[s])} psi[r ^ flip[s]]
+ * psi / out: complex amplitudes as separate fp32 real and imaginary arrays of
+ * N entries (out must not overlap psi); flip / sign / ny: int32 [S] (flip: X or
+ * Y on qubit k sets bit k, sign: Y or Z, ny: number of Y factors, used mod 4),
+ * coeff: fp32 [S]. Bits of flip at or above K are ignored. 0 <= K <= 30.
+ * Replaces native_apply / pauli_partial_kernel / pauli_reduce_kernel
+ * (pauli.py:296-578) in one launch with no partial arrays.
+ * ---------------------------------------------------------------------- */
+LSR_API int lsr_pauli_apply_f32(const float* psi_r, const float* psi_i, const int* flip, const int* sign,
+                                const int* ny, const float* coeff, float* out_r, float* out_i, int K, int S,
+                                lsr_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Shampoo / SOAP on stacks of equally shaped parameter blocks

@@ -150,12 +150,39 @@ def test_native_reconstruct_general_shapes():
     assert rel_fro(W.cpu().numpy(), ref) < TOL_F32
 
 
-def test_kron_sum_out_dense_operator_follows_factor_updates():
-    """Small factors run through a cached dense operator W = sum_s A_s (x) B_s: an in-place change of
-    the factors (a new version of the tensor) must be seen by the next call."""
+def test_kron_small_path_matches_fp64():
+    """Small fp32 problems run as one FFMA launch (no workspace): the reference's 64 x 8 shape at its
+    sweep's sizes, ragged batches (not a multiple of the 16 right-hand sides per block), row counts
+    that are not a multiple of 16, every supported n, A given transposed (kron_sum_out's `at`) or
+    not (kron_apply), S from 1 to 8."""
     import lsr.kron as K
+    from lsr import _lib
+    lib = _lib.load()
+    g = torch.Generator(device="cuda").manual_seed(31)
+    cases = [(256, 64, 8, 1), (1024, 64, 8, 8), (4096, 64, 8, 2), (1, 64, 8, 3), (300, 64, 8, 4),
+             (17, 48, 4, 3), (100, 20, 16, 2), (129, 64, 1, 2), (5, 64, 2, 8), (33, 7, 8, 5)]
+    for M, m, n, S in cases:
+        assert lib.lsr_kron_apply_workspace_bytes(M, m, n, S, 1) == 0, (M, m, n, S)  # the small path
+        x = torch.randn(M, m, n, device="cuda", generator=g)
+        A = torch.randn(S, m, m, device="cuda", generator=g) / m ** 0.5
+        b = torch.randn(S, n, n, device="cuda", generator=g) / n ** 0.5
+        ref = torch.einsum("sik,mkl,sjl->mij", A.double(), x.double(), b.double()).cpu().numpy()
+        out = torch.full_like(x, float("nan"))
+        K.kron_sum_out(x, A.transpose(1, 2).contiguous(), b, out)
+        assert rel_fro(out.cpu().numpy(), ref) < TOL_F32, (M, m, n, S)
+        Y = K.kron_apply(x, A, b)
+        assert rel_fro(Y.cpu().numpy(), ref) < TOL_F32, (M, m, n, S)
+
+
+def test_kron_sum_out_dense_operator_follows_factor_updates():
+    """Small factors with many right-hand sides run through a cached dense operator
+    W = sum_s A_s (x) B_s: an in-place change of the factors (a new version of the tensor) must be
+    seen by the next call."""
+    import lsr.kron as K
+    from lsr import _lib
+    assert _lib.load().lsr_kron_apply_workspace_bytes(20000, 64, 8, 4, 1) > 0  # not the small path
     g = torch.Generator(device="cuda").manual_seed(77)
-    x = torch.randn(300, 64, 8, device="cuda", generator=g)
+    x = torch.randn(20000, 64, 8, device="cuda", generator=g)
     at = torch.randn(4, 64, 64, device="cuda", generator=g) / 8
     b = torch.randn(4, 8, 8, device="cuda", generator=g) / 3
     out = torch.empty_like(x)
