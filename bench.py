@@ -313,8 +313,9 @@ def run_lsr(args) -> None:
     del M
 
     # ---------------------------------------------------------------- device-timed
-    for _ in range(args.warmup):
-        step()
+    with _nvtx("muon.warmup"):
+        for _ in range(args.warmup):
+            step()
     barrier(world)
     sampler = ClockSampler(physical_gpu(local_rank))
     sampler.start()
@@ -325,8 +326,9 @@ def run_lsr(args) -> None:
     barrier(world)
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_start.record()
-    for _ in range(args.steps):
-        step()
+    with _nvtx("muon.steps"):
+        for _ in range(args.steps):
+            step()
     t_end.record()
     barrier(world)
     launches = _lib.launch_count() - launches0
@@ -808,10 +810,17 @@ def run_workload(args) -> None:
                 ms_s = _time_gpu(lambda: (torch.linalg.eigh(Ls), torch.linalg.eigh(Rs)), 1, 1, flush_bytes=0)
                 t_eigh += ms_s * len(grp.refs) / k
                 n_eigh += 2 * k
+
+            def torch_refresh():  # the same refresh through torch: cuBLAS bmm + cuSOLVER batched QR
+                for _, grp, _ in opt._groups:
+                    for S_, Q_ in ((grp.L, grp.QLf), (grp.R, grp.QRf)):
+                        torch.linalg.qr(torch.bmm(S_, Q_))
+            ms_tq = _time_gpu(torch_refresh, 1, 1)
             lines.append({"workload": f"refresh: SOAP eigenbasis refresh of the config-5 blocks ({args.layers} layers, "
                                       f"{nfac} factors of <= 1024^2), one power iteration + Householder QR",
                           "value": ms, "unit": "ms", "torch_eigh_fp32_ms_extrapolated": t_eigh,
-                          "eigh_sample_factors": n_eigh, "speedup_vs_eigh": t_eigh / ms})
+                          "eigh_sample_factors": n_eigh, "speedup_vs_eigh": t_eigh / ms,
+                          "torch_bmm_qr_fp32_ms": ms_tq, "speedup_vs_torch_qr": ms_tq / ms})
         else:
             gq = torch.Generator(device=dev).manual_seed(5)
             for (r, c), grp, _ in opt._groups:  # stand-ins with the shapes of the inverse roots

@@ -5,12 +5,15 @@
 //   kron : out[n][j] = decay[n] state[n][j] + KA[j / NE][ea[n]] KE[j % NE][et[n]]
 //          (K = KA ⊗ KE, D = NA NE, never formed)
 // HBM-bound: 8 bytes per state entry (read state, write out) plus the K column
-// (dense: D floats per stream, mostly from L2; kron: two factor entries per
-// output, from L1). One warp per stream row: the row moves as 16-byte vectors,
-// 512 contiguous bytes per warp instruction, the stream's event, decay and
-// factor column offsets are loaded once per row. An event index outside
-// [0, D) (dense) or [0, NA) x [0, NE) (kron) is not read: the row is written as
-// NaN and ST_EVENT_INDEX is recorded in the device status word.
+// (dense: D floats per stream, mostly from L2; kron: the row's column of KA
+// and of KE, NA + NE floats staged once per row in the warp's shared memory).
+// One warp per stream row: the row moves as 16-byte vectors, 512 contiguous
+// bytes per warp instruction; the stream's event and decay are loaded once per
+// row. An event index outside [0, D) (dense) or [0, NA) x [0, NE) (kron) is
+// not read: the row is written as NaN and ST_EVENT_INDEX is recorded in the
+// device status word.
+#include <atomic>
+
 #include "runtime.cuh"
 
 namespace lsr {
@@ -22,6 +25,11 @@ constexpr int ST_EVENT_INDEX = 110;
 
 __device__ __forceinline__ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// Shared floats per warp for the staged Kronecker path (0: factors too large, gather instead).
+__host__ __device__ __forceinline__ int hsm_floats_per_warp(int na, int ne) {
+  return (long long)na + ne <= 2048 ? na + ne : 0;
+}
+
 template <bool KRON>
 __global__ void __launch_bounds__(HK_THREADS) hawkes_kernel(const float* __restrict__ state,
                                                             const int* __restrict__ event,
@@ -30,8 +38,12 @@ __global__ void __launch_bounds__(HK_THREADS) hawkes_kernel(const float* __restr
                                                             const float* __restrict__ K0,
                                                             const float* __restrict__ K1, float* __restrict__ out,
                                                             int n, int d, int na, int ne, int* status) {
+  extern __shared__ float hsm[];  // kron: per warp, the row's KA column (na) and KE column (ne)
   const int lane = threadIdx.x & 31;
   const bool vec = (d % 4 == 0) && al16(state) && al16(out) && (KRON || al16(K0));
+  const bool staged = KRON && hsm_floats_per_warp(na, ne) > 0;
+  float* wa = staged ? hsm + (threadIdx.x >> 5) * (na + ne) : nullptr;
+  float* we = staged ? wa + na : nullptr;
   for (long long row = (long long)blockIdx.x * HK_WARPS + (threadIdx.x >> 5); row < n;
        row += (long long)gridDim.x * HK_WARPS) {
     const float dec = __ldg(decay + row);
@@ -43,6 +55,36 @@ __global__ void __launch_bounds__(HK_THREADS) hawkes_kernel(const float* __restr
     if (!ok) {
       if (lane == 0) set_status(status, ST_EVENT_INDEX);
       for (int j = lane; j < d; j += 32) o[j] = __int_as_float(0x7fc00000);
+      continue;
+    }
+    if (staged) {
+      // column e0 of KA and column e1 of KE, once per row; then every entry is two shared reads
+      __syncwarp();  // the previous row's reads of wa / we are done
+      for (int a = lane; a < na; a += 32) wa[a] = __ldg(K0 + (long long)a * na + e0);
+      for (int e = lane; e < ne; e += 32) we[e] = __ldg(K1 + (long long)e * ne + e1);
+      __syncwarp();
+      if (vec) {
+        for (int j = 4 * lane; j < d; j += 128) {
+          const float4 sv = __ldcs(reinterpret_cast<const float4*>(s + j));
+          float k[4];
+          int a = j / ne, e = j - a * ne;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            k[t] = wa[a] * we[e];
+            if (++e == ne) {
+              e = 0;
+              ++a;
+            }
+          }
+          __stcs(reinterpret_cast<float4*>(o + j), make_float4(fmaf(dec, sv.x, k[0]), fmaf(dec, sv.y, k[1]),
+                                                               fmaf(dec, sv.z, k[2]), fmaf(dec, sv.w, k[3])));
+        }
+      } else {
+        for (int j = lane; j < d; j += 32) {
+          const int a = j / ne, e = j - a * ne;
+          o[j] = fmaf(dec, s[j], wa[a] * we[e]);
+        }
+      }
       continue;
     }
     if (vec) {
@@ -88,9 +130,19 @@ int launch_hawkes(const float* state, const int* event, const int* event_type, c
   if (!status) return LSR_ERR_LAUNCH;
   const long long rows_per_wave = (long long)HK_WARPS * 8 * device_sm_count();
   const int blocks = (int)std::min<long long>((n + HK_WARPS - 1) / HK_WARPS, rows_per_wave / HK_WARPS);
+  const size_t smem = KRON ? (size_t)HK_WARPS * hsm_floats_per_warp(na, ne) * sizeof(float) : 0;
+  if (smem > 48 * 1024) {
+    static std::atomic<int> attr_set{0};
+    if (!attr_set.load(std::memory_order_relaxed)) {
+      if (cudaFuncSetAttribute(hawkes_kernel<KRON>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               HK_WARPS * 2048 * (int)sizeof(float)) != cudaSuccess)
+        return LSR_ERR_LAUNCH;
+      attr_set.store(1, std::memory_order_relaxed);
+    }
+  }
   ProfScope prof(PK_EW_OTHER, st);
-  hawkes_kernel<KRON><<<blocks, HK_THREADS, 0, st>>>(state, event, event_type, decay, K0, K1, out, n, d, na, ne,
-                                                     status);
+  hawkes_kernel<KRON><<<blocks, HK_THREADS, smem, st>>>(state, event, event_type, decay, K0, K1, out, n, d, na, ne,
+                                                        status);
   return cudaGetLastError() == cudaSuccess ? LSR_OK : LSR_ERR_LAUNCH;
 }
 

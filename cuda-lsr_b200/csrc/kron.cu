@@ -523,13 +523,29 @@ __global__ void __launch_bounds__(KS_THREADS) kron_small_kernel(const float* __r
       } else {
         tv[0] = T[k * NW + cg];
       }
-#pragma unroll
-      for (int r = 0; r < RI; ++r) {
-        const int i = ig * RI + r;
-        const float a = i < m ? Ac[k * m + i] : 0.f;
-#pragma unroll
-        for (int c = 0; c < CPT; ++c) acc[r][c] = fmaf(a, tv[c], acc[r][c]);
+      float av[RI];
+      bool done = false;
+      if constexpr (RI == 4) {
+        if (m == 64) {  // the thread's four rows are one aligned 16-byte vector
+          const float4 a4 = *reinterpret_cast<const float4*>(Ac + k * 64 + ig * 4);
+          av[0] = a4.x;
+          av[1] = a4.y;
+          av[2] = a4.z;
+          av[3] = a4.w;
+          done = true;
+        }
       }
+      if (!done) {
+#pragma unroll
+        for (int r = 0; r < RI; ++r) {
+          const int i = ig * RI + r;
+          av[r] = i < m ? Ac[k * m + i] : 0.f;
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < RI; ++r)
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) acc[r][c] = fmaf(av[r], tv[c], acc[r][c]);
     }
     if (more) {
       float* An = As + (cur ^ 1) * mm;

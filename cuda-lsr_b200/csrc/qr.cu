@@ -81,16 +81,30 @@ __device__ __forceinline__ void qr_block_sum32(float (&acc)[32], float* red, flo
 
 // Block-reflector update of column pairs of a trailing matrix C (m rows, row
 // stride n): C -= V X (V^T C), X = T^T (factorization: H_1 ... H_w applied
-// transposed) or X = T (forming Q). V is the panel in shared memory: unit
-// lower-trapezoidal, V[i][k] = P[i][k] for i > k, 1 on the diagonal, 0 above.
-// Each thread owns columns c and c + QR_THREADS, so every broadcast read of a
-// V row feeds two FMA chains; the rows below the 32-row triangle go in
+// transposed) or X = T (forming Q). V [m][32] is in shared memory with rows of
+// 32 floats (16-byte aligned) and its unit lower-trapezoidal form written out
+// (ones on the diagonal, zeros above), so every row is read as eight 16-byte
+// broadcasts and no row needs a select. Each thread owns columns c and
+// c + QR_THREADS, so every V value read feeds two FMA chains; rows go in
 // batches of QR_ROWB, their loads issued together (the matrix streams from L2 /
 // DRAM: one load in flight per thread would leave the kernel latency-bound).
 constexpr int QR_ROWB = 8;
+constexpr int QR_VLD = 32;  // row stride of the compacted V
+
+__device__ __forceinline__ void v_row(const float* V, int i, float (&v)[32]) {
+  const float4* r4 = reinterpret_cast<const float4*>(V + i * QR_VLD);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 t = r4[q];
+    v[4 * q] = t.x;
+    v[4 * q + 1] = t.y;
+    v[4 * q + 2] = t.z;
+    v[4 * q + 3] = t.w;
+  }
+}
 
 template <bool TRANS_T>
-__device__ __forceinline__ void wy_update_cols(float* C, int n, int m, int ncols, int w, const float* P,
+__device__ __forceinline__ void wy_update_cols(float* C, int n, int m, int ncols, int w, const float* V,
                                                const float* Ts) {
   for (int c0 = threadIdx.x; c0 < ncols; c0 += 2 * QR_THREADS) {
     const int c1 = c0 + QR_THREADS;
@@ -100,18 +114,7 @@ __device__ __forceinline__ void wy_update_cols(float* C, int n, int m, int ncols
     float a0[32], a1[32];
 #pragma unroll
     for (int k = 0; k < 32; ++k) a0[k] = a1[k] = 0.f;
-    const int mt = min(m, QR_NB);
-    for (int i = 0; i < mt; ++i) {  // the triangle
-      const float x0 = col0[(size_t)i * n], x1 = col1[(size_t)i * n];
-      const float* row = P + i * QR_LDP;
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        const float v = k < i ? row[k] : (k == i ? 1.f : 0.f);
-        a0[k] = fmaf(v, x0, a0[k]);
-        a1[k] = fmaf(v, x1, a1[k]);
-      }
-    }
-    int i = mt;
+    int i = 0;
     for (; i + QR_ROWB <= m; i += QR_ROWB) {
       float x0[QR_ROWB], x1[QR_ROWB];
 #pragma unroll
@@ -121,22 +124,23 @@ __device__ __forceinline__ void wy_update_cols(float* C, int n, int m, int ncols
       }
 #pragma unroll
       for (int u = 0; u < QR_ROWB; ++u) {
-        const float* row = P + (i + u) * QR_LDP;
+        float v[32];
+        v_row(V, i + u, v);
 #pragma unroll
         for (int k = 0; k < 32; ++k) {
-          const float v = row[k];
-          a0[k] = fmaf(v, x0[u], a0[k]);
-          a1[k] = fmaf(v, x1[u], a1[k]);
+          a0[k] = fmaf(v[k], x0[u], a0[k]);
+          a1[k] = fmaf(v[k], x1[u], a1[k]);
         }
       }
     }
     for (; i < m; ++i) {
       const float x0 = col0[(size_t)i * n], x1 = col1[(size_t)i * n];
-      const float* row = P + i * QR_LDP;
+      float v[32];
+      v_row(V, i, v);
 #pragma unroll
       for (int k = 0; k < 32; ++k) {
-        a0[k] = fmaf(row[k], x0, a0[k]);
-        a1[k] = fmaf(row[k], x1, a1[k]);
+        a0[k] = fmaf(v[k], x0, a0[k]);
+        a1[k] = fmaf(v[k], x1, a1[k]);
       }
     }
     // y = X a in place (T upper triangular): T^T a needs a[0..k] for y[k], so
@@ -167,19 +171,7 @@ __device__ __forceinline__ void wy_update_cols(float* C, int n, int m, int ncols
       }
     }
     // C[i] -= sum_k V[i][k] y[k]
-    for (int r = 0; r < mt; ++r) {
-      const float* row = P + r * QR_LDP;
-      float d0 = 0.f, d1 = 0.f;
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        const float v = k < r ? row[k] : (k == r ? 1.f : 0.f);
-        d0 = fmaf(v, a0[k], d0);
-        d1 = fmaf(v, a1[k], d1);
-      }
-      col0[(size_t)r * n] -= d0;
-      if (has1) col1[(size_t)r * n] -= d1;
-    }
-    int r = mt;
+    int r = 0;
     for (; r + QR_ROWB <= m; r += QR_ROWB) {
       float x0[QR_ROWB], x1[QR_ROWB];
 #pragma unroll
@@ -189,28 +181,53 @@ __device__ __forceinline__ void wy_update_cols(float* C, int n, int m, int ncols
       }
 #pragma unroll
       for (int u = 0; u < QR_ROWB; ++u) {
-        const float* row = P + (r + u) * QR_LDP;
+        float v[32];
+        v_row(V, r + u, v);
         float d0 = 0.f, d1 = 0.f;
 #pragma unroll
         for (int k = 0; k < 32; ++k) {
-          d0 = fmaf(row[k], a0[k], d0);
-          d1 = fmaf(row[k], a1[k], d1);
+          d0 = fmaf(v[k], a0[k], d0);
+          d1 = fmaf(v[k], a1[k], d1);
         }
         col0[(size_t)(r + u) * n] = x0[u] - d0;
         if (has1) col1[(size_t)(r + u) * n] = x1[u] - d1;
       }
     }
     for (; r < m; ++r) {
-      const float* row = P + r * QR_LDP;
+      float v[32];
+      v_row(V, r, v);
       float d0 = 0.f, d1 = 0.f;
 #pragma unroll
       for (int k = 0; k < 32; ++k) {
-        d0 = fmaf(row[k], a0[k], d0);
-        d1 = fmaf(row[k], a1[k], d1);
+        d0 = fmaf(v[k], a0[k], d0);
+        d1 = fmaf(v[k], a1[k], d1);
       }
       col0[(size_t)r * n] -= d0;
       if (has1) col1[(size_t)r * n] -= d1;
     }
+  }
+}
+
+// Rewrites the factored panel P ([m][QR_LDP]: V below the diagonal) in place as
+// the compacted V [m][QR_VLD] with its unit lower-trapezoidal form written out.
+// Chunks of 32 rows go in order, each read completely before it is written:
+// chunk c's destination ends below chunk c+1's source (1024 (c+1) <= 1056 (c+1)).
+__device__ __forceinline__ void compact_panel(float* P, int m, int w) {
+  for (int c0 = 0; c0 < m; c0 += 32) {
+    float v[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int idx = threadIdx.x + q * QR_THREADS, i = c0 + idx / 32, k = idx % 32;
+      v[q] = 0.f;
+      if (i < m && k < w) v[q] = k < i ? P[i * QR_LDP + k] : (k == i ? 1.f : 0.f);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int idx = threadIdx.x + q * QR_THREADS, i = c0 + idx / 32, k = idx % 32;
+      if (i < m) P[i * QR_VLD + k] = v[q];
+    }
+    __syncthreads();
   }
 }
 
@@ -289,7 +306,10 @@ __global__ void __launch_bounds__(QR_THREADS, 1) qr_factor_kernel(float* A, floa
     for (int idx = tid; idx < QR_NB * QR_NB; idx += QR_THREADS)
       T[((size_t)b * npan + p) * QR_NB * QR_NB + idx] = Ts[(idx / QR_NB) * QR_LDP + idx % QR_NB];
     // trailing matrix: A2 (rows c0.., cols c0+w..) -= V T^T (V^T A2)
-    wy_update_cols<true>(Ab + (size_t)c0 * n + c0 + w, n, m, n - c0 - w, w, P, Ts);
+    if (n - c0 - w > 0) {
+      compact_panel(P, m, w);
+      wy_update_cols<true>(Ab + (size_t)c0 * n + c0 + w, n, m, n - c0 - w, w, P, Ts);
+    }
     __syncthreads();
   }
 }
@@ -310,7 +330,7 @@ __global__ void __launch_bounds__(QR_THREADS, 1) qr_form_q_kernel(const float* A
     const int c0 = p * QR_NB, w = min(QR_NB, n - c0), m = n - c0;
     for (int idx = tid; idx < m * QR_NB; idx += QR_THREADS) {
       const int i = idx / QR_NB, j = idx % QR_NB;
-      P[i * QR_LDP + j] = (j < w && i > j) ? Ab[(size_t)(c0 + i) * n + c0 + j] : 0.f;
+      P[i * QR_VLD + j] = j < w ? (i > j ? Ab[(size_t)(c0 + i) * n + c0 + j] : (i == j ? 1.f : 0.f)) : 0.f;
     }
     for (int idx = tid; idx < QR_NB * QR_NB; idx += QR_THREADS)
       Ts[(idx / QR_NB) * QR_LDP + idx % QR_NB] = T[((size_t)b * npan + p) * QR_NB * QR_NB + idx];
