@@ -32,9 +32,7 @@ constexpr int kMaxSeg = 6;
 constexpr int BM = 128;
 constexpr int BK = 64;       // bf16 elements in one 128-byte swizzle row (one K block)
 constexpr int BK_TF32 = 32;  // fp32 (tf32) elements in one 128-byte swizzle row
-constexpr int kGemmThreads = 192;
 constexpr int kTileRing = 8;  // tile indices in flight between the producer and the consumers
-constexpr int kEpiThreads = 128;
 
 // Epilogue modes.
 enum : int {
@@ -348,6 +346,25 @@ struct EpiT {
   static constexpr bool AUX = (EPI == EPI_NS_POLY || EPI == EPI_NS_UPDATE || EPI == EPI_F32_EMA);
 };
 
+// Epilogue warps per CTA. The SOAP epilogue (Adam on the rotated gradient) moves
+// 20 bytes of moments and output per element and walks its chunks one after
+// another; it runs 8 warps, the two warps of each TMEM lane quarter taking
+// alternate 32-column chunks. Every other epilogue runs 4.
+template <int EPI>
+constexpr int epi_warps() {
+  return EPI == EPI_SOAP_ADAM ? 8 : 4;
+}
+template <int EPI>
+constexpr int gemm_threads() {
+  return 64 + 32 * epi_warps<EPI>();  // producer warp, MMA warp, epilogue warps
+}
+// Staging chunks per epilogue warp: 2 direct + 2 transposed; the SOAP epilogue
+// stages only the accumulator (double-buffered).
+template <int EPI>
+constexpr int epi_slots() {
+  return EPI == EPI_SOAP_ADAM ? 2 : 4;
+}
+
 template <int ROWB>
 __device__ __forceinline__ uint32_t stg_off(int r, int j) {
   if constexpr (ROWB == 64)
@@ -381,11 +398,9 @@ __device__ __forceinline__ void aux_prefetch(const GroupDesc& G, int b, int row0
 
 // Adam moments of one 32 x 32 chunk for the EPI_SOAP_ADAM epilogue, held in
 // registers: lane l owns the 16-byte vectors (row (l / 8) + 4 i, columns 4 (l % 8)
-// .. + 3) for i < 8, so m and v move in coalesced 128-byte row segments. The
-// epilogue loads the NEXT live chunk's moments while it processes the current
-// one (512 bytes in flight per lane), which keeps the moment stream going while
-// the accumulator is read out, staged and the results stored. Empty for the
-// other epilogues.
+// .. + 3) for i < 8, so m and v move in coalesced 128-byte row segments. They
+// are loaded while the chunk's accumulator columns come out of TMEM. Empty for
+// the other epilogues.
 template <int EPI>
 struct MomentChunk {
   __device__ __forceinline__ void load(const GroupDesc&, int, int, int, int) {}
@@ -418,7 +433,7 @@ __device__ __forceinline__ void epilogue_chunk_staged(const GemmParams& p, int g
   using T = EpiT<EPI>;
   if constexpr (EPI == EPI_SOAP_ADAM) {
     // Work row-contiguously: 8 lanes per row, 16-byte vectors, so m / v / u move
-    // in coalesced segments; this chunk's moments were loaded one chunk ahead.
+    // in coalesced segments.
     const int jv = lane & 7;
     __syncwarp();  // the previous chunk's reads of dbuf are done
 #pragma unroll
@@ -667,7 +682,7 @@ struct GemmSmem {
   static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * 128 * KS;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;
-  static constexpr int EPI_BYTES = (kEpiThreads / 32) * 4 * EpiT<EPI>::CHB;  // per warp: 2 direct + 2 transposed
+  static constexpr int EPI_BYTES = epi_warps<EPI>() * epi_slots<EPI>() * EpiT<EPI>::CHB;
   static constexpr int BAR_OFFSET = EPI_OFFSET + EPI_BYTES;
   static constexpr int BAR_BYTES = 8 * (2 * STAGES + 5 + 2 * kTileRing) + 16 + 4 * kTileRing;
   static constexpr int TOTAL = BAR_OFFSET + BAR_BYTES + 1024;  // + alignment slack
@@ -701,7 +716,7 @@ constexpr int default_stages() {
 // the TMA operations and barrier round trips per flop halve; the MMA thread
 // issues 8 UMMAs per stage (4 when the segment's last stage holds one block).
 template <int BN, int STAGES, int EPI, int TF32, int DUAL, int PAIR, int KS = 1>
-__global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(gemm_threads<EPI>(), 1) gemm_sm100_kernel(const __grid_constant__ GemmParams p) {
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 32 in [64, 256]");
   constexpr int KE = TF32 ? BK_TF32 : BK;        // elements per K block (= MN elements per MN-major chunk)
   constexpr int CHUNK = KE * 128 * KS;           // bytes of one MN-major chunk (KS KE K-rows of 128 B)
@@ -736,9 +751,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
-  // Consumers of one tile-ring slot: the MMA thread and the four epilogue
-  // warps of the leader, plus (pair) the peer's producer and epilogue warps.
-  constexpr uint32_t kTileConsumers = PAIR ? 10u : 5u;
+  // Consumers of one tile-ring slot: the MMA thread and the epilogue warps of
+  // the leader, plus (pair) the peer's producer and epilogue warps.
+  constexpr int EW = epi_warps<EPI>();
+  constexpr uint32_t kTileConsumers = (PAIR ? 2u : 1u) * (1u + (uint32_t)EW);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -747,7 +763,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull + a, 1);
-      mbar_init(tempty + a, kEpiThreads * (PAIR ? 2 : 1));
+      mbar_init(tempty + a, 32 * EW * (PAIR ? 2 : 1));
     }
     mbar_init(done_bar, 1);
     for (int r = 0; r < kTileRing; ++r) {
@@ -1030,7 +1046,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    uint8_t* ebase = smem + L::EPI_OFFSET + (warp - 2) * 4 * ET::CHB;
+    // with 8 epilogue warps, warps 2-5 take the even and warps 6-9 the odd chunks
+    const uint32_t chunk_mask = EW == 8 ? ((warp - 2) >= 4 ? 0xAAAAAAAAu : 0x55555555u) : 0xFFFFFFFFu;
+    uint8_t* ebase = smem + L::EPI_OFFSET + (warp - 2) * epi_slots<EPI>() * ET::CHB;
     int acc = 0;
     uint32_t aph = 0;
     uint32_t kchunk = 0;  // chunks processed by this warp (staging buffer parity)
@@ -1066,16 +1084,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
           const int col0 = tj * BN + cc * 32;
           if (col0 < G.N && !(G.tri && col0 < row0)) live |= 1u << cc;
         }
+        live &= chunk_mask;
       }
       uint4 pre[ET::VPR];
 #pragma unroll
       for (int i = 0; i < ET::VPR; ++i) pre[i] = make_uint4(0u, 0u, 0u, 0u);
       if constexpr (ET::AUX) {
         if (G.tma_out && live) aux_prefetch<EPI>(G, b, row0, tj * BN + (__ffs(live) - 1) * 32, lane, pre);
-      }
-      MomentChunk<EPI> mom_next;
-      if constexpr (EPI == EPI_SOAP_ADAM) {
-        if (live) mom_next.load(G, b, row0, tj * BN + (__ffs(live) - 1) * 32, lane);
       }
       if (!mbar_wait(tfull + acc, aph, abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
@@ -1106,10 +1121,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_sm100_kernel(const __gri
           if constexpr (ET::AUX) {
             if (rem) aux_prefetch<EPI>(G, b, row0, tj * BN + (__ffs(rem) - 1) * 32, lane, pre);
           }
-          const MomentChunk<EPI> mom = mom_next;
-          if constexpr (EPI == EPI_SOAP_ADAM) {
-            if (rem) mom_next.load(G, b, row0, tj * BN + (__ffs(rem) - 1) * 32, lane);
-          }
+          MomentChunk<EPI> mom;
+          mom.load(G, b, row0, col0, lane);  // in flight while the accumulator chunk arrives
           tmem_ld_wait();
           uint8_t* dbuf = ebase + (kchunk & 1) * ET::CHB;
           uint8_t* tbuf = ebase + (2 + (kchunk & 1)) * ET::CHB;

@@ -100,18 +100,24 @@ bool kron_use_dense(int m, int n) {
   return mn <= kDenseMaxMN && mn % 4 == 0;
 }
 
-// Small fp32 problems (m <= 64, n in {1, 2, 4, 8, 16}, at most kSmallMaxFlop):
-// one FFMA launch with no workspace (kron_small_kernel). Here the tensor-core
-// paths are bound by latency, not by the math: the dense operator's GEMM has a
-// handful of 128 x 256 tiles, each walking 3 x (m n / 32) K blocks in series
-// (measured on the reference's x [M, 64, 8] sweep: a 31 us floor per call for
-// M <= 1024, against 2 (m n)(m + n) S M flops that take a few us on every SM).
-constexpr double kSmallMaxFlop = 1.0e9;
+// Small fp32 problems (m <= 64, n in {1, 2, 4, 8, 16}): one FFMA launch with no
+// workspace (kron_small_kernel) when a cost model says it beats the dense
+// operator's tensor-core GEMM. The model was fitted on B200 to the reference's
+// x [M, 64, 8] sweep (M 256..16384, S 1..8; microseconds per call):
+//   small ≈ 4 + (X + Y bytes) / 2 TB/s + S (2.2 + term flops / 22 TFLOP/s)
+//   dense ≈ max(31, 18.6 + 3xTF32 flops / 452 TFLOP/s)
+// The FFMA kernel pays a latency per term; the dense GEMM has a launch floor and
+// a handful of 128 x 256 tiles whose K loop runs 3 (m n / 32) blocks in series.
 constexpr int KS_THREADS = 256;
 
 bool kron_use_small(int batch, int m, int n, int nterms) {
   if (m > 64 || n > 16 || 32 % n) return false;
-  return 2.0 * batch * nterms * m * n * (double)(m + n) <= kSmallMaxFlop;
+  const double mn = (double)m * n;
+  const double small_us = 4.0 + 8.0 * batch * mn / 2.0e6 +
+                          nterms * (2.2 + 2.0 * batch * mn * (m + n) / 22.0e6);
+  if (mn > kDenseMaxMN || (m * n) % 4) return true;  // no dense path for these factors
+  const double dense_us = std::max(31.0, 18.6 + 6.0 * batch * mn * mn / 452.0e6);
+  return small_us < dense_us;
 }
 
 // W[(i n + j)][(k n + l)] = sum_s A_s[i][k] B_s[j][l]  (A_s[i][k] = at[s][k][i] when a_trans),

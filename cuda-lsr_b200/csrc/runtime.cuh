@@ -211,7 +211,7 @@ inline int launch_gemm(GemmParams& p, cudaStream_t st, int kind = PK_GEMM_OTHER)
     const int clusters = std::min(device_sm_count() / 2, p.total_tiles);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(2 * clusters);
-    cfg.blockDim = dim3(kGemmThreads);
+    cfg.blockDim = dim3(gemm_threads<EPI>());
     cfg.dynamicSmemBytes = L::TOTAL;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -224,7 +224,7 @@ inline int launch_gemm(GemmParams& p, cudaStream_t st, int kind = PK_GEMM_OTHER)
     if (cudaLaunchKernelEx(&cfg, kfn, p) != cudaSuccess) return LSR_ERR_LAUNCH;
   } else {
     const int grid = std::min(device_sm_count(), p.total_tiles);
-    kfn<<<grid, kGemmThreads, L::TOTAL, st>>>(p);
+    kfn<<<grid, gemm_threads<EPI>(), L::TOTAL, st>>>(p);
   }
   return cudaGetLastError() == cudaSuccess ? LSR_OK : LSR_ERR_LAUNCH;
 }

@@ -260,9 +260,11 @@ LSR_API int lsr_kron_sum_f32(const float* A, const float* X, const float* B, flo
  * Each term is two chained GEMMs (the cheaper association first); the
  * intermediate is kept as a hi + lo pair so the second product stays at fp32
  * accuracy.  _bf16: bf16 operands.  _f32: fp32 operands (3xTF32).
- * Small fp32 problems (m <= 64, n in {1, 2, 4, 8, 16}, at most 1e9 flops, e.g.
- * the reference's x [M, 64, 8] sweep up to M S ~ 13000) run as one fp32 FFMA
- * launch instead: the workspace size is then 0 and ws may be NULL.
+ * Small fp32 problems (m <= 64, n in {1, 2, 4, 8, 16}) run as one fp32 FFMA
+ * launch instead when a cost model fitted on B200 predicts it faster than the
+ * tensor-core path (the reference's x [M, 64, 8] sweep: M <= 256 up to S = 8,
+ * M = 1024 up to S = 4, M = 4096 at S = 1): the workspace size is then 0 and ws
+ * may be NULL.
  * ---------------------------------------------------------------------- */
 LSR_API size_t lsr_kron_apply_workspace_bytes(int batch, int m, int n, int nterms, int f32);
 /* Small-factor Kronecker apply split in two, for callers that apply the same

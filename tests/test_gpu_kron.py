@@ -151,16 +151,16 @@ def test_native_reconstruct_general_shapes():
 
 
 def test_kron_small_path_matches_fp64():
-    """Small fp32 problems run as one FFMA launch (no workspace): the reference's 64 x 8 shape at its
-    sweep's sizes, ragged batches (not a multiple of the 16 right-hand sides per block), row counts
+    """Small fp32 problems run as one FFMA launch (no workspace): the reference's 64 x 8 shape at the
+    sweep sizes where that launch is chosen, ragged batches (not a multiple of the 16 right-hand sides per block), row counts
     that are not a multiple of 16, every supported n, A given transposed (kron_sum_out's `at`) or
     not (kron_apply), S from 1 to 8."""
     import lsr.kron as K
     from lsr import _lib
     lib = _lib.load()
     g = torch.Generator(device="cuda").manual_seed(31)
-    cases = [(256, 64, 8, 1), (1024, 64, 8, 8), (4096, 64, 8, 2), (1, 64, 8, 3), (300, 64, 8, 4),
-             (17, 48, 4, 3), (100, 20, 16, 2), (129, 64, 1, 2), (5, 64, 2, 8), (33, 7, 8, 5)]
+    cases = [(256, 64, 8, 1), (256, 64, 8, 8), (1024, 64, 8, 4), (4096, 64, 8, 1), (1, 64, 8, 3),
+             (300, 64, 8, 4), (17, 48, 4, 3), (100, 20, 16, 2), (129, 64, 1, 2), (5, 64, 2, 8), (33, 7, 8, 5)]
     for M, m, n, S in cases:
         assert lib.lsr_kron_apply_workspace_bytes(M, m, n, S, 1) == 0, (M, m, n, S)  # the small path
         x = torch.randn(M, m, n, device="cuda", generator=g)
