@@ -85,10 +85,12 @@ __device__ __forceinline__ void momentum8(const float (&g)[8], float (&buf)[8], 
 //             (muon_lm_ddp.py:388-401: the norm is a bf16 scalar);
 //   phase 2 — one 64x128 tile of X: X = bf16(X / nrm)  (X.div_(norm)).
 // Within a group, matrix k's phase-2 tiles follow matrix k+L's phase-1 tiles
-// (L = the lag: roughly 24 MB of X), so a matrix is finished long before its
-// scale tiles are claimed and its X is still in L2 when it is rescaled: the
-// normalisation costs almost no DRAM traffic, and DRAM sees the 8 bytes per
-// parameter of the momentum/orient pass only (read g, buf; write buf, X).
+// (L = the lag: roughly 16 MB of X), so a matrix is finished before its scale
+// tiles are claimed and part of its X is still in L2 when it is rescaled: DRAM
+// sees the 8 bytes per parameter of the momentum/orient pass (read g, buf;
+// write buf, X) plus the rescale's L2 misses. Lags of 8, 16, 24, 32 and 48 MB
+// measured 4.6, 4.55, 4.76, 4.79 and 4.82 ms per GPT-2-XL step: a shorter lag
+// keeps more of X in L2, until the scale tiles start waiting for norms.
 // Every phase-2 tile's wait is for phase-1 tiles claimed earlier from the same
 // counter, i.e. already running, so it ends; it is bounded all the same
 // (LSR_WAIT_TIMEOUT_NS, then a status code and the tile is skipped).
@@ -645,7 +647,7 @@ int run_prologue(NsGroup* gs, const ProSource* srcs, int ng, const Control& ctl,
       G.p2_c = cdiv(S.n, P2_COLS);
       G.S = cdiv(S.m, P2_ROWS) * G.p2_c;
       const double xbytes = 2.0 * S.m * S.ldn;
-      G.L = (int)std::min<double>(S.batch, std::max(1.0, std::ceil(32.0 * (1 << 20) / xbytes)));
+      G.L = (int)std::min<double>(S.batch, std::max(1.0, std::ceil(16.0 * (1 << 20) / xbytes)));
       G.vec = (src.C % 8 == 0) && (!src.trans || src.R % 8 == 0);  // and 16-byte bases, checked per matrix
       G.partials = S.partials;
       G.nrm = S.nrm;
