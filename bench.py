@@ -486,6 +486,9 @@ def run_e2e(args, params, grads, step, world, opt):
     for _ in range(max(1, min(args.warmup, 2))):
         e2e_step()
     compute.wait_event(ev_down)
+    # the first timed step's gradients (uploaded during the last warm-up step) are on the device:
+    # the timed region then holds exactly n uploads, n steps and n downloads
+    compute.wait_stream(up)
     barrier(world)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n = max(1, min(args.steps, 5))
