@@ -104,7 +104,7 @@ bool kron_use_dense(int m, int n) {
 // workspace (kron_small_kernel) when a cost model says it beats the dense
 // operator's tensor-core GEMM. The model was fitted on B200 to the reference's
 // x [M, 64, 8] sweep (M 256..16384, S 1..8; microseconds per call):
-//   small ≈ 4 + (X + Y bytes) / 2 TB/s + S (2.2 + term flops / 22 TFLOP/s)
+//   small ≈ 4 + (X + Y bytes) / 2.2 TB/s + S (1.2 + term flops / 26 TFLOP/s)
 //   dense ≈ max(31, 18.6 + 3xTF32 flops / 452 TFLOP/s)
 // The FFMA kernel pays a latency per term; the dense GEMM has a launch floor and
 // a handful of 128 x 256 tiles whose K loop runs 3 (m n / 32) blocks in series.
@@ -113,8 +113,8 @@ constexpr int KS_THREADS = 256;
 bool kron_use_small(int batch, int m, int n, int nterms) {
   if (m > 64 || n > 16 || 32 % n) return false;
   const double mn = (double)m * n;
-  const double small_us = 4.0 + 8.0 * batch * mn / 2.0e6 +
-                          nterms * (2.2 + 2.0 * batch * mn * (m + n) / 22.0e6);
+  const double small_us = 4.0 + 8.0 * batch * mn / 2.2e6 +
+                          nterms * (1.2 + 2.0 * batch * mn * (m + n) / 26.0e6);
   if (mn > kDenseMaxMN || (m * n) % 4) return true;  // no dense path for these factors
   const double dense_us = std::max(31.0, 18.6 + 6.0 * batch * mn * mn / 452.0e6);
   return small_us < dense_us;
@@ -450,49 +450,53 @@ int kron_apply_dense_f32(const void* A, int a_trans, const void* X, const void* 
 
 // Small Kronecker apply, fp32 FFMA: Y[b] = sum_s A_s X[b] B_s^T for X [batch][m][n].
 // A block takes NW / n right-hand sides (their X staged in shared memory once)
-// and a band of mb output rows (all m, or half of them when the grid would
-// otherwise leave SMs idle: blockIdx.y picks the band). Per term s it forms
-// T = [X_0 B_s^T | ... ] (m x NW) in shared memory and adds A_s[band] T into a
-// register tile (RI rows x CPT columns per thread, NW = 16 CPT), so the sum over
-// s stays in registers and Y is written once. Only the band's rows of A_{s+1}
-// and B_{s+1} are loaded into registers while term s computes and stored into the
-// other half of a double buffer, so no term waits for a global load. Lanes 0-15 /
-// 16-31 of a warp take adjacent column groups of two row groups: every read of T
-// is one wavefront and the A reads are broadcasts.
-constexpr int KS_MAXM = 64, KS_PRE = KS_MAXM * KS_MAXM / KS_THREADS;  // A_s elements per thread (at most)
+// and all m <= 64 rows. Per term s it forms T = [X_0 B_s^T | ... ] (m x NW) in
+// shared memory and adds A_s T into a register tile (RI rows x CPT columns per
+// thread, NW = 16 CPT), so the sum over s stays in registers and Y is written
+// once. A_{s+1} and B_{s+1} are loaded into registers while term s computes
+// and stored into the other half of a double buffer, so no term waits for a
+// global load. Lanes 0-15 / 16-31 of a warp take adjacent column groups of two
+// row groups: every read of T is one wavefront and the A reads are broadcasts.
+constexpr int KS_MAXM = 64, KS_PRE = KS_MAXM * KS_MAXM / KS_THREADS;  // A_s elements per thread
+
+// Per-snapshot stride of the staged X: m n + 1 (the snapshots of a block start in
+// distinct banks), or m n + 4 for n = 8, where rows are read as 16-byte vectors
+// (the four snapshots of a 32-column block then start 4 banks apart).
+__host__ __device__ __forceinline__ int ks_xstride(int m, int n) { return m * n + (n == 8 ? 4 : 1); }
 
 template <int RI, int CPT>
 __global__ void __launch_bounds__(KS_THREADS) kron_small_kernel(const float* __restrict__ A, int a_trans,
                                                                 const float* __restrict__ X,
                                                                 const float* __restrict__ B, float* __restrict__ Y,
-                                                                int batch, int m, int n, int S, int mb) {
+                                                                int batch, int m, int n, int S) {
   extern __shared__ __align__(16) float ksm[];
   constexpr int NW = 16 * CPT;
-  const int P = NW / n, xs = m * n + 1;  // padded per-snapshot stride: the P snapshots sit in distinct banks
-  const int am = m * mb, nn = n * n;     // band of A_s: am elements, As[k][il] = A_s[i0 + il][k]
-  const int i0 = blockIdx.y * mb, iend = min(m, i0 + mb);
+  const int P = NW / n, xs = ks_xstride(m, n);
+  const int mm = m * m, nn = n * n;
   float* Xs = ksm;                       // [P][m n (+1)]
   float* T = Xs + ((P * xs + 3) & ~3);   // [m][NW]
-  float* As = T + m * NW;                // [2][m (k)][mb (il)]
-  float* Bs = As + 2 * am;               // [2][n][n]
+  float* As = T + m * NW;                // [2][m (k)][m (i)]: As[k][i] = A_s[i][k]
+  float* Bs = As + 2 * mm;               // [2][n][n]
   const int m0 = blockIdx.x * P;
   const int np = min(P, batch - m0);
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int cg = lane & 15;              // column group: columns CPT cg ..
-  const int ig = (lane >> 4) + 2 * w;    // row group: band rows RI ig ..
+  const int ig = (lane >> 4) + 2 * w;    // row group: rows RI ig ..
+  // T[k][c] = sum_l X_p[k][l] B_s[j][l]: NW divides the block, so this thread's
+  // column tc (snapshot tp, B row tj) is the same for every k it forms
+  const int tc = tid % NW, tp = tc / n, tj = tc - tp * n;
   const long long xo = (long long)m0 * m * n;
   for (int e = tid; e < P * m * n; e += KS_THREADS) {
     const int p = e / (m * n), q = e - p * (m * n);
     Xs[p * xs + q] = p < np ? X[xo + e] : 0.f;
   }
-  // element e of As (k = e / mb, row i0 + e % mb) from term s; rows past m read as zero
+  // element e of As (k = e / m, i = e % m) from term s
   auto a_elem = [&](int s, int e) -> float {
-    const int k = e / mb, i = i0 + (e - k * mb);
-    if (i >= m) return 0.f;
-    const float* src = A + (size_t)s * m * m;
-    return a_trans ? __ldg(src + (size_t)k * m + i) : __ldg(src + (size_t)i * m + k);
+    const int k = e / m, i = e - k * m;
+    const float* src = A + (size_t)s * mm;
+    return a_trans ? __ldg(src + e) : __ldg(src + (size_t)i * m + k);
   };
-  for (int e = tid; e < am; e += KS_THREADS) As[e] = a_elem(0, e);
+  for (int e = tid; e < mm; e += KS_THREADS) As[e] = a_elem(0, e);
   for (int e = tid; e < nn; e += KS_THREADS) Bs[e] = __ldg(B + e);
   float acc[RI][CPT];
 #pragma unroll
@@ -502,7 +506,7 @@ __global__ void __launch_bounds__(KS_THREADS) kron_small_kernel(const float* __r
   __syncthreads();
   for (int s = 0; s < S; ++s) {
     const int cur = s & 1;
-    const float* Ac = As + cur * am;
+    const float* Ac = As + cur * mm;
     const float* Bc = Bs + cur * nn;
     float pre[KS_PRE], preb = 0.f;
     const bool more = s + 1 < S;
@@ -510,17 +514,30 @@ __global__ void __launch_bounds__(KS_THREADS) kron_small_kernel(const float* __r
 #pragma unroll
       for (int q = 0; q < KS_PRE; ++q) {
         const int e = tid + q * KS_THREADS;
-        pre[q] = e < am ? a_elem(s + 1, e) : 0.f;
+        pre[q] = e < mm ? a_elem(s + 1, e) : 0.f;
       }
       if (tid < nn) preb = __ldg(B + (size_t)(s + 1) * nn + tid);
     }
-    for (int e = tid; e < m * NW; e += KS_THREADS) {
-      const int k = e / NW, c = e - k * NW, p = c / n, j = c - p * n;
-      const float* xr = Xs + p * xs + k * n;
-      const float* br = Bc + j * n;
-      float t = 0.f;
-      for (int l = 0; l < n; ++l) t = fmaf(xr[l], br[l], t);
-      T[e] = t;
+    {
+      float br[16];  // row tj of B_s (n <= 16), read once per term
+#pragma unroll
+      for (int l = 0; l < 16; ++l) br[l] = l < n ? Bc[tj * n + l] : 0.f;
+      const float* xp = Xs + tp * xs;
+      for (int k = tid / NW; k < m; k += KS_THREADS / NW) {
+        const float* xr = xp + k * n;
+        float t = 0.f;
+        if (n == 8) {  // xs and k n are multiples of 4: two aligned 16-byte reads
+          const float4 x0 = *reinterpret_cast<const float4*>(xr);
+          const float4 x1 = *reinterpret_cast<const float4*>(xr + 4);
+          t = fmaf(x0.x, br[0], fmaf(x0.y, br[1], fmaf(x0.z, br[2], x0.w * br[3])));
+          t += fmaf(x1.x, br[4], fmaf(x1.y, br[5], fmaf(x1.z, br[6], x1.w * br[7])));
+        } else {
+#pragma unroll
+          for (int l = 0; l < 16; ++l)
+            if (l < n) t = fmaf(xr[l], br[l], t);
+        }
+        T[k * NW + tc] = t;
+      }
     }
     __syncthreads();
 #pragma unroll 4
@@ -536,7 +553,7 @@ __global__ void __launch_bounds__(KS_THREADS) kron_small_kernel(const float* __r
       float av[RI];
       bool done = false;
       if constexpr (RI == 4) {
-        if (mb == 64) {  // the thread's four rows are one aligned 16-byte vector
+        if (m == 64) {  // the thread's four rows are one aligned 16-byte vector
           const float4 a4 = *reinterpret_cast<const float4*>(Ac + k * 64 + ig * 4);
           av[0] = a4.x;
           av[1] = a4.y;
@@ -545,19 +562,11 @@ __global__ void __launch_bounds__(KS_THREADS) kron_small_kernel(const float* __r
           done = true;
         }
       }
-      if constexpr (RI == 2) {
-        if (mb == 32) {  // two rows: one aligned 8-byte vector
-          const float2 a2 = *reinterpret_cast<const float2*>(Ac + k * 32 + ig * 2);
-          av[0] = a2.x;
-          av[1] = a2.y;
-          done = true;
-        }
-      }
       if (!done) {
 #pragma unroll
         for (int r = 0; r < RI; ++r) {
-          const int il = ig * RI + r;
-          av[r] = il < mb ? Ac[k * mb + il] : 0.f;
+          const int i = ig * RI + r;
+          av[r] = i < m ? Ac[k * m + i] : 0.f;
         }
       }
 #pragma unroll
@@ -566,11 +575,11 @@ __global__ void __launch_bounds__(KS_THREADS) kron_small_kernel(const float* __r
         for (int c = 0; c < CPT; ++c) acc[r][c] = fmaf(av[r], tv[c], acc[r][c]);
     }
     if (more) {
-      float* An = As + (cur ^ 1) * am;
+      float* An = As + (cur ^ 1) * mm;
 #pragma unroll
       for (int q = 0; q < KS_PRE; ++q) {
         const int e = tid + q * KS_THREADS;
-        if (e < am) An[e] = pre[q];
+        if (e < mm) An[e] = pre[q];
       }
       if (tid < nn) Bs[(cur ^ 1) * nn + tid] = preb;
     }
@@ -578,8 +587,8 @@ __global__ void __launch_bounds__(KS_THREADS) kron_small_kernel(const float* __r
   }
 #pragma unroll
   for (int r = 0; r < RI; ++r) {
-    const int i = i0 + ig * RI + r;
-    if (ig * RI + r >= mb || i >= iend) continue;
+    const int i = ig * RI + r;
+    if (i >= m) continue;
 #pragma unroll
     for (int c = 0; c < CPT; ++c) {
       const int col = CPT * cg + c, p = col / n, j = col - p * n;
@@ -590,14 +599,14 @@ __global__ void __launch_bounds__(KS_THREADS) kron_small_kernel(const float* __r
 
 template <int RI, int CPT>
 int launch_small(const float* A, int a_trans, const float* X, const float* B, float* Y, int batch, int m, int n,
-                 int S, int bands, cudaStream_t st) {
+                 int S, cudaStream_t st) {
   static std::atomic<int> attr_set{0};
   constexpr int NW = 16 * CPT;
-  const int P = NW / n, mb = cdiv(m, bands);
+  const int P = NW / n;
   const size_t smem =
-      ((size_t)((P * (m * n + 1) + 3) & ~3) + (size_t)m * NW + 2 * (size_t)m * mb + 2 * (size_t)n * n) * 4;
-  constexpr int kMaxSmem = 64 * 1024;  // m <= 64, n <= 16: at most 32 (64 + 1) + 64 x 32 + 2 (4096 + 256) floats
-  if (smem > (size_t)kMaxSmem || mb > 16 * RI) return LSR_ERR_SHAPE;
+      ((size_t)((P * ks_xstride(m, n) + 3) & ~3) + (size_t)m * NW + 2 * (size_t)m * m + 2 * (size_t)n * n) * 4;
+  constexpr int kMaxSmem = 64 * 1024;  // m <= 64, n <= 16: at most 32 (64 + 4) + 64 x 32 + 2 (4096 + 256) floats
+  if (smem > (size_t)kMaxSmem) return LSR_ERR_SHAPE;
   if (!attr_set.load(std::memory_order_relaxed)) {
     if (cudaFuncSetAttribute(kron_small_kernel<RI, CPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
         cudaSuccess)
@@ -605,35 +614,29 @@ int launch_small(const float* A, int a_trans, const float* X, const float* B, fl
     attr_set.store(1, std::memory_order_relaxed);
   }
   ProfScope prof(PK_GEMM_OTHER, st);
-  kron_small_kernel<RI, CPT><<<dim3(cdiv(batch, P), bands), KS_THREADS, smem, st>>>(A, a_trans, X, B, Y, batch, m, n,
-                                                                                   S, mb);
+  kron_small_kernel<RI, CPT><<<cdiv(batch, P), KS_THREADS, smem, st>>>(A, a_trans, X, B, Y, batch, m, n, S);
   return launch_ok();
 }
 
-// RI = band rows per thread = mb / 16, rounded up (16 row groups per block).
+// 32-column blocks (two columns per thread) once there are enough right-hand sides
+// to give every SM two blocks; 16-column blocks below that, so small batches
+// still spread over the GPU. RI = rows per thread = m / 16, rounded up.
 template <int CPT>
 int small_rows(const float* A, int a_trans, const float* X, const float* B, float* Y, int batch, int m, int n, int S,
-               int bands, cudaStream_t st) {
-  switch (cdiv(cdiv(m, bands), 16)) {
-    case 1: return launch_small<1, CPT>(A, a_trans, X, B, Y, batch, m, n, S, bands, st);
-    case 2: return launch_small<2, CPT>(A, a_trans, X, B, Y, batch, m, n, S, bands, st);
-    case 3: return launch_small<3, CPT>(A, a_trans, X, B, Y, batch, m, n, S, bands, st);
-    default: return launch_small<4, CPT>(A, a_trans, X, B, Y, batch, m, n, S, bands, st);
+               cudaStream_t st) {
+  switch (cdiv(m, 16)) {
+    case 1: return launch_small<1, CPT>(A, a_trans, X, B, Y, batch, m, n, S, st);
+    case 2: return launch_small<2, CPT>(A, a_trans, X, B, Y, batch, m, n, S, st);
+    case 3: return launch_small<3, CPT>(A, a_trans, X, B, Y, batch, m, n, S, st);
+    default: return launch_small<4, CPT>(A, a_trans, X, B, Y, batch, m, n, S, st);
   }
 }
 
-// 32-column blocks (two columns per thread) once there are enough right-hand sides
-// to give every SM two blocks, 16-column blocks below that, so small batches still
-// spread over the GPU; the rows split into two bands while the grid has fewer than
-// four blocks per SM (each band forms T again: m NW n more FMAs, 1 / m_band of the
-// term's work).
 int kron_apply_small_f32(const float* A, int a_trans, const float* X, const float* B, float* Y, int batch, int m,
                          int n, int S, cudaStream_t st) {
-  const int sms = device_sm_count();
-  const int cpt = (n <= 16 && 16 % n == 0 && cdiv(batch, 16 / n) < 2 * sms) ? 1 : 2;
-  const int bands = (m >= 32 && cdiv(batch, 16 * cpt / n) < 4 * sms) ? 2 : 1;
-  return cpt == 1 ? small_rows<1>(A, a_trans, X, B, Y, batch, m, n, S, bands, st)
-                  : small_rows<2>(A, a_trans, X, B, Y, batch, m, n, S, bands, st);
+  if (n <= 16 && 16 % n == 0 && cdiv(batch, 16 / n) < 2 * device_sm_count())
+    return small_rows<1>(A, a_trans, X, B, Y, batch, m, n, S, st);
+  return small_rows<2>(A, a_trans, X, B, Y, batch, m, n, S, st);
 }
 
 int kron_apply(const void* A, int a_trans, const void* X, const void* B, float* Y, int batch, int m, int n,
