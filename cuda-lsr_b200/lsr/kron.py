@@ -87,17 +87,30 @@ def _dense_operator(A3, B3, a_trans: bool):
     return _DENSE_CACHE[key]
 
 
+# Workspace bytes of lsr_kron_apply per (batch, m, n, S, fp32): a function of the sizes only
+# (0 selects the small-problem path), looked up once per shape instead of once per call.
+_WS_BYTES: dict = {}
+
+
 def _kron_apply(X3, A3, B3, a_trans: bool, Y) -> None:
     batch, m, n = X3.shape
     S = A3.shape[0]
     f32 = X3.dtype == torch.float32
     lib = _lib.load()
-    nb = lib.lsr_kron_apply_workspace_bytes(batch, m, n, S, int(f32))
+    key = (batch, m, n, S, f32)
+    nb = _WS_BYTES.get(key)
+    if nb is None:
+        nb = lib.lsr_kron_apply_workspace_bytes(batch, m, n, S, int(f32))
+        if len(_WS_BYTES) >= 256:
+            _WS_BYTES.clear()
+        _WS_BYTES[key] = nb
     if f32 and nb == 0:  # small problem: one FFMA launch inside liblsr, no workspace
-        with _lib.on_device(X3.device):
+        dev = X3.device
+        with _lib.on_device(dev):
             rc = lib.lsr_kron_apply_f32(A3.data_ptr(), int(a_trans), X3.data_ptr(), B3.data_ptr(), Y.data_ptr(),
-                                        batch, m, n, S, None, 0, _lib.stream_handle(X3.device))
-        _lib.check(rc, "lsr_kron_apply")
+                                        batch, m, n, S, None, 0, _lib.stream_handle(dev))
+        if rc:
+            _lib.check(rc, "lsr_kron_apply")
         return
     if f32 and m * n <= _DENSE_MAX_MN and (m * n) % 4 == 0:
         with _lib.on_device(X3.device):
