@@ -133,7 +133,8 @@ def test_coupled_newton_matches_reference_golden():
 
 
 def test_gpt2xl_soap_blocks():
-    """Config 5's blocking: 42 blocks per layer, 2016 in total, the survey's shape counts."""
+    """GPT-2-XL blocked at max_preconditioner_dim 1024: 42 blocks per layer in 10 block shapes,
+    2016 blocks over the 48 layers."""
     import collections
     from oracle import shampoo as osh
     assert osh.block_sizes(1600, 1024) == [1024, 576]
