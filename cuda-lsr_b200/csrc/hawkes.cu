@@ -58,14 +58,32 @@ __global__ void __launch_bounds__(HK_THREADS) hawkes_kernel(const float* __restr
       continue;
     }
     if (staged) {
-      // column e0 of KA and column e1 of KE, once per row; then every entry is two shared reads
+      // column e0 of KA and column e1 of KE, once per row; then every entry is two shared reads.
+      // The row's first 1024 state entries are requested before the columns are gathered, so
+      // their DRAM latency overlaps the gather.
+      constexpr int HK_PRE = 8;  // 16-byte vectors per lane issued ahead
+      float4 svp[HK_PRE];
+      if (vec) {
+#pragma unroll
+        for (int u = 0; u < HK_PRE; ++u) {
+          const int j = 4 * lane + 128 * u;
+          if (j < d) svp[u] = __ldcs(reinterpret_cast<const float4*>(s + j));
+        }
+      }
       __syncwarp();  // the previous row's reads of wa / we are done
       for (int a = lane; a < na; a += 32) wa[a] = __ldg(K0 + (long long)a * na + e0);
       for (int e = lane; e < ne; e += 32) we[e] = __ldg(K1 + (long long)e * ne + e1);
       __syncwarp();
       if (vec) {
-        for (int j = 4 * lane; j < d; j += 128) {
-          const float4 sv = __ldcs(reinterpret_cast<const float4*>(s + j));
+        for (int j = 4 * lane, u = 0; j < d; j += 128, ++u) {
+          float4 sv;
+          if (u < HK_PRE) {
+#pragma unroll
+            for (int q = 0; q < HK_PRE; ++q)
+              if (q == u) sv = svp[q];
+          } else {
+            sv = __ldcs(reinterpret_cast<const float4*>(s + j));
+          }
           float k[4];
           int a = j / ne, e = j - a * ne;
 #pragma unroll
