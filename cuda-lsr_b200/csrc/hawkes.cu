@@ -105,7 +105,32 @@ __global__ void __launch_bounds__(HK_THREADS) hawkes_kernel(const float* __restr
       }
       continue;
     }
-    if (vec) {
+    if (!KRON && vec) {
+      // dense: each 1024-entry segment of the row and of the K column is loaded in full before
+      // any of it is stored (safe with out == state: every entry is read before it is written),
+      // so eight 16-byte vectors of each are in flight per lane
+      const float* kc = K0 + (long long)e0 * d;
+      constexpr int HD = 8;
+      for (int j0 = 0; j0 < d; j0 += 128 * HD) {
+        float4 sv[HD], kv[HD];
+#pragma unroll
+        for (int u = 0; u < HD; ++u) {
+          const int j = j0 + 4 * lane + 128 * u;
+          if (j < d) {
+            sv[u] = __ldcs(reinterpret_cast<const float4*>(s + j));
+            kv[u] = __ldg(reinterpret_cast<const float4*>(kc + j));
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < HD; ++u) {
+          const int j = j0 + 4 * lane + 128 * u;
+          if (j < d)
+            __stcs(reinterpret_cast<float4*>(o + j),
+                   make_float4(fmaf(dec, sv[u].x, kv[u].x), fmaf(dec, sv[u].y, kv[u].y),
+                               fmaf(dec, sv[u].z, kv[u].z), fmaf(dec, sv[u].w, kv[u].w)));
+        }
+      }
+    } else if (vec) {
       const float* kc = KRON ? nullptr : K0 + (long long)e0 * d;
       for (int j = 4 * lane; j < d; j += 128) {
         const float4 sv = __ldcs(reinterpret_cast<const float4*>(s + j));
