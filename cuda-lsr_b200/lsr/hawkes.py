@@ -27,6 +27,11 @@ def _check(t: torch.Tensor, name: str, dtype: torch.dtype) -> None:
         raise ValueError(f"{name} must be contiguous")
 
 
+def _same_device(*ts: torch.Tensor) -> None:
+    if any(t.device != ts[0].device for t in ts[1:]):
+        raise ValueError("all tensors must be on the same CUDA device")
+
+
 def _events(e: torch.Tensor, name: str, n: int) -> torch.Tensor:
     if e.dtype == torch.int64:
         e = e.to(torch.int32)
@@ -47,6 +52,7 @@ def hawkes_dense(state: torch.Tensor, event: torch.Tensor, decay: torch.Tensor, 
     event = _events(event, "event", N)
     if decay.shape != (N,) or Kcol.shape != (D, D) or out.shape != (N, D):
         raise ValueError(f"decay must be [{N}], Kcol [{D}, {D}] and out [{N}, {D}]")
+    _same_device(state, event, decay, Kcol, out)
     lib = _lib.load()
     with _lib.on_device(state.device):
         rc = lib.lsr_hawkes_dense_f32(state.data_ptr(), event.data_ptr(), decay.data_ptr(), Kcol.data_ptr(),
@@ -73,6 +79,7 @@ def hawkes_kron(state: torch.Tensor, event_asset: torch.Tensor, event_type: torc
     event_type = _events(event_type, "event_type", N)
     if decay.shape != (N,) or out.shape != (N, D):
         raise ValueError(f"decay must be [{N}] and out [{N}, {D}]")
+    _same_device(state, event_asset, event_type, decay, KA, KE, out)
     lib = _lib.load()
     with _lib.on_device(state.device):
         rc = lib.lsr_hawkes_kron_f32(state.data_ptr(), event_asset.data_ptr(), event_type.data_ptr(),

@@ -63,6 +63,8 @@ def pauli_apply(psi_r, psi_i, flip, sign, ny, coeff, out_r=None, out_i=None):
         for src in (psi_r, psi_i):
             if o.data_ptr() == src.data_ptr():
                 raise ValueError("out must not alias psi")
+    if any(t.device != psi_r.device for t in (psi_i, *ints, coeff, out_r, out_i)):
+        raise ValueError("all tensors must be on the same CUDA device")
     lib = _lib.load()
     with _lib.on_device(psi_r.device):
         rc = lib.lsr_pauli_apply_f32(psi_r.data_ptr(), psi_i.data_ptr(), ints[0].data_ptr(), ints[1].data_ptr(),
