@@ -27,3 +27,13 @@ def test_oracle_mask_form_matches_kronecker_form():
         psi = rng.standard_normal(1 << K) + 1j * rng.standard_normal(1 << K)
         f, s, y = op.encode(ops)
         assert np.abs(op.apply(psi, f, s, y, coeff) - op.dense(ops, coeff) @ psi).max() < 1e-12
+
+
+def test_wrapper_rejects_host_tensors():
+    import pytest
+    import torch
+    from lsr import pauli as LP
+    psi = torch.zeros(8)
+    m = torch.zeros(2, dtype=torch.int32)
+    with pytest.raises(ValueError, match="CUDA"):
+        LP.pauli_apply(psi, psi.clone(), m, m, m, torch.ones(2))
