@@ -186,11 +186,12 @@ def native_reconstruct(factors, K, out=None, block=256):
     S = factors[0].shape[0]
     rows, cols = [], []
     for f in factors:
-        _check(f, "factor")
-        if f.dtype != torch.float32 or f.dim() != 3 or f.shape[0] != S:
+        if not (f.is_cuda and f.dtype == torch.float32 and f.dim() == 3 and f.is_contiguous()) or f.shape[0] != S:
+            _check(f, "factor")  # the CUDA / dtype / layout message first, as for any operand
             raise RuntimeError("factors must be float32 [S, r, c] with a common S")
-        rows.append(f.shape[1])
-        cols.append(f.shape[2])
+        _, r, c = f.shape
+        rows.append(r)
+        cols.append(c)
     R = 1
     C = 1
     for r, c in zip(rows, cols):
@@ -200,11 +201,21 @@ def native_reconstruct(factors, K, out=None, block=256):
         out = torch.empty(R, C, dtype=torch.float32, device=factors[0].device)
     if out.dtype != torch.float32 or not out.is_contiguous() or out.numel() != R * C:
         raise RuntimeError(f"out must be a contiguous float32 tensor with {R}x{C} elements")
-    ptrs = (ctypes.c_void_p * K)(*[f.data_ptr() for f in factors])
-    rr = (ctypes.c_int * K)(*rows)
-    cc = (ctypes.c_int * K)(*cols)
+    key = (tuple(f.data_ptr() for f in factors), tuple(rows), tuple(cols))
+    arrs = _RECON_ARGS.get(key)
+    if arrs is None:  # the factor address and shape arrays, built once per factor set
+        arrs = ((ctypes.c_void_p * K)(*key[0]), (ctypes.c_int * K)(*rows), (ctypes.c_int * K)(*cols))
+        if len(_RECON_ARGS) >= 64:
+            _RECON_ARGS.clear()
+        _RECON_ARGS[key] = arrs
     lib = _lib.load()
-    with _lib.on_device(out.device):
-        rc = lib.lsr_kron_reconstruct_f32(ptrs, rr, cc, K, S, out.data_ptr(), _lib.stream_handle(out.device))
-    _lib.check(rc, "lsr_kron_reconstruct_f32")
+    dev = out.device
+    with _lib.on_device(dev):
+        rc = lib.lsr_kron_reconstruct_f32(arrs[0], arrs[1], arrs[2], K, S, out.data_ptr(), _lib.stream_handle(dev))
+    if rc:
+        _lib.check(rc, "lsr_kron_reconstruct_f32")
     return out
+
+
+# ctypes argument arrays of native_reconstruct per (factor addresses, row counts, column counts).
+_RECON_ARGS: dict = {}
