@@ -142,3 +142,21 @@ def test_peer_push_argument_checks_without_gpu():
     assert lib.lsr_peer_push(None, 3, d, 1, 0, None) == -1    # odd byte count
     assert lib.lsr_peer_push(None, 0, d, 1, 0, None) == 0     # nothing to do
     assert lib.lsr_ipc_open(None, None) == -1
+
+
+def test_small_kronecker_routing_follows_the_measured_faster_path():
+    """fp32 Kronecker apply on the reference's x [M, 64, 8] sweep: workspace 0 selects the one-launch
+    FFMA kernel, anything else the dense-operator tensor-core GEMM. The routing is the fitted cost
+    model's; these are the cases where each path measured faster on a B200 (same-box sweeps with
+    every case forced onto each path)."""
+    from lsr import _lib
+    lib = _lib.load()
+    small = {(256, s) for s in (1, 2, 4, 8)} | {(1024, s) for s in (1, 2, 4)} | {(4096, 1)}
+    for M in (256, 1024, 4096, 16384):
+        for S in (1, 2, 4, 8):
+            nb = lib.lsr_kron_apply_workspace_bytes(M, 64, 8, S, 1)
+            assert (nb == 0) == ((M, S) in small), (M, S, nb)
+    # m n not a multiple of 4 has no dense-operator path: the FFMA kernel at any size
+    assert lib.lsr_kron_apply_workspace_bytes(100000, 7, 1, 8, 1) == 0
+    # n above 16 has no FFMA kernel
+    assert lib.lsr_kron_apply_workspace_bytes(4, 64, 32, 2, 1) > 0
