@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(KS_THREADS) kron_small_kernel(const float* __r
   constexpr int NW = 16 * CPT;
   const int P = NW / n, xs = ks_xstride(m, n);
   const int mm = m * m, nn = n * n;
-  float* Xs = ksm;                       // [P][m n (+1)]
+  float* Xs = ksm;                       // [P][xs]
   float* T = Xs + ((P * xs + 3) & ~3);   // [m][NW]
   float* As = T + m * NW;                // [2][m (k)][m (i)]: As[k][i] = A_s[i][k]
   float* Bs = As + 2 * mm;               // [2][n][n]
@@ -605,7 +605,7 @@ int launch_small(const float* A, int a_trans, const float* X, const float* B, fl
   const int P = NW / n;
   const size_t smem =
       ((size_t)((P * ks_xstride(m, n) + 3) & ~3) + (size_t)m * NW + 2 * (size_t)m * m + 2 * (size_t)n * n) * 4;
-  constexpr int kMaxSmem = 64 * 1024;  // m <= 64, n <= 16: at most 32 (64 + 4) + 64 x 32 + 2 (4096 + 256) floats
+  constexpr int kMaxSmem = 64 * 1024;  // m <= 64, n <= 16: at most 32 (64 + 1) + 64 x 32 + 2 (4096 + 256) floats
   if (smem > (size_t)kMaxSmem) return LSR_ERR_SHAPE;
   if (!attr_set.load(std::memory_order_relaxed)) {
     if (cudaFuncSetAttribute(kron_small_kernel<RI, CPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
